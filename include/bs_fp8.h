@@ -1,0 +1,110 @@
+/* C-ABI of the B200 (sm_100a) block-scaled FP8 linear path.
+ *
+ * Everything here takes plain device pointers, sizes and a CUDA stream passed as void*, returns
+ * 0 or a positive error code, and never throws. Kernels run asynchronously on the given stream;
+ * nothing allocates or synchronises except where a comment says so.
+ *
+ * Data formats (all row-major, all on one device):
+ *   A   e4m3 activations [M, K]                    (K % 128 == 0, 16-byte aligned base)
+ *   As  fp32 activation group scales [M, K/128]    (one scale per token and 128-wide K group)
+ *   B   e4m3 weights, either row-major [N, K] or "tile-first" [N/128][K/128][128][128]
+ *       (bs_fp8_pack_tiles makes the latter)
+ *   Bs  fp32 weight block scales [N/128, K/128]    (one scale per 128x128 block)
+ *   C   bf16 or fp32 output [M, ldc], columns 0..N-1 written
+ *   Q   e4m3 quantised SiLU(gate)*up [M, N/2], Qs fp32 group scales [M, N/256]
+ *
+ * Reference interfaces are cited as path:line inside lexing-2026/ucloud-ai-infra;
+ * "H" is patches/fp8_hand_sm89.py.
+ */
+#ifndef BS_FP8_H
+#define BS_FP8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define BS_OK 0
+#define BS_ERR_ARG 1          /* a shape, stride or dtype argument is outside the contract   */
+#define BS_ERR_ALIGN 2        /* a pointer or row stride breaks the 16-byte alignment rule     */
+#define BS_ERR_WORKSPACE 3    /* workspace missing or smaller than bs_fp8_workspace_bytes()    */
+#define BS_ERR_TMAP 4         /* cuTensorMapEncodeTiled is unavailable or rejected the tensor  */
+#define BS_ERR_CUDA 5         /* a CUDA runtime call failed (launch, attribute, device query)  */
+#define BS_ERR_BUILD 6        /* a kernel's register count does not match its setmaxnreg split */
+#define BS_ERR_TIMEOUT_FULL 101     /* device status: bounded wait on a TMA stage ran out       */
+#define BS_ERR_TIMEOUT_EMPTY 102    /* device status: bounded wait for a free stage ran out     */
+#define BS_ERR_TIMEOUT_PFULL 103    /* device status: bounded wait for an MMA partial ran out   */
+#define BS_ERR_TIMEOUT_PEMPTY 104   /* device status: bounded wait for a TMEM buffer ran out    */
+#define BS_ERR_TIMEOUT_DRAIN 105    /* device status: teardown drain ran out                    */
+#define BS_ERR_TIMEOUT_SELFTEST 199 /* device status: the self-test wait ran out (expected)     */
+
+/* Block-scaled FP8 GEMM:  C[m, n] = sum_kb (A[m, kb] . B[n, kb]) * As[m, kb] * Bs[n/128, kb].
+ * Replaces the launch inside H:704-719 (`matmul(A, B, C, As, Bs, M, N, K, block_size)`, kernel
+ * `fp8_gemm_hand(pA, pB, pC, pAs, pBs, M, N, G)` at H:104-105) and the Triton
+ * `w8a8_block_fp8_matmul_triton(A, B, As, Bs, block_size, output_dtype)` it hooks
+ * (patches/apply_sglang_fp8_hand_gemm.py:26-33).
+ *   b_tiled    1 if B is tile-first (H:667 layout), 0 if row-major [N, K]
+ *   out_dtype  0 = bf16 (the reference's only output), 1 = fp32 (tensor-parallel partials)
+ *   ldc        output row stride in elements, >= N, multiple of 8
+ * M <= 128 runs the swap-AB split-K decode kernel and needs `workspace` of at least
+ * bs_fp8_workspace_bytes(M, N, K, 0) bytes, zero-filled before its first use (the kernel
+ * leaves it in that state). M > 128 needs no workspace. M == 0 is a no-op. */
+int bs_fp8_gemm(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
+                int ldc, int b_tiled, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused MLP front half: gate_up GEMM -> SiLU(gate) * up -> per-token-group e4m3 quant.
+ * B holds N2 = 2*I weight rows, gate rows first (I % 128 == 0). Writes Q [M, I] and Qs [M, I/128]
+ *   y = silu(g) * u;  Qs = max(amax_128(|y|), 1e-10) / 448;  Q = sat_e4m3(y * (1 / Qs)).
+ * Replaces kernel `fp8_gemm_silu_quant(pA, pB, pQ, pAs, pBs, pQs, M, N, G)` (H:341-342,
+ * epilogue H:532-579) launched by `fused_gate_up(proj, x)` (H:675-701). Same workspace rule as
+ * bs_fp8_gemm, with bs_fp8_workspace_bytes(M, N2, K, 1). */
+int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* As, const float* Bs, float* Qs,
+                           int M, int N2, int K, int b_tiled, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Workspace bytes the decode kernels need for (M, N, K); 0 when M > 128 or M == 0. */
+size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused);
+
+/* Per-token-group activation quant: x bf16 [M, K] (row stride ldx elements, multiple of 8) ->
+ * A e4m3 [M, K], As fp32 [M, K/128] with As = max(amax_128(|x|) / 448, 1e-12), A = e4m3(x / As).
+ * Replaces SGLang's `per_token_group_quant_fp8(x, 128)` called at H:690-693, with the
+ * arithmetic of the reference's torch quantiser (scripts/fp8_gemm_factor_check.py:22-27). */
+int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K, void* stream);
+
+/* Tile-first weight pre-pack: tiles[nb][kb][r][c] = W[nb*128 + r][kb*128 + c] for e4m3 W [N, K].
+ * Replaces the permute in `relayout(model)` (H:667). W and tiles must not overlap. */
+int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream);
+
+/* Reads the device status word of the current device (synchronises the device). Writes the
+ * code to *code and clears it when `clear` is non-zero. Counterpart of the reference's
+ * RuntimeError on driver failures (H:630, :634, :649); here kernels report bounded-wait
+ * timeouts through it. */
+int bs_fp8_status(int* code, int clear);
+
+/* Runs one tiny kernel whose mbarrier wait is never satisfied and must give up after
+ * `limit_ns`, leaving BS_ERR_TIMEOUT_SELFTEST in the status word. Exercises the bounded-wait
+ * path without any fault. No reference counterpart (the reference has no bounded waits). */
+int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
+/* Number of SMs the kernels size their persistent grids for (current device). */
+int bs_fp8_num_sms(void);
+
+/* Human-readable text for a status code. */
+const char* bs_fp8_error_string(int code);
+
+/* ABI version of this library (bumped when a signature changes). */
+int bs_fp8_abi_version(void);
+
+/* Text of the last CUDA runtime failure (BS_ERR_CUDA) seen on the calling thread: which call
+ * failed and the runtime's error name. Empty when none. Counterpart of the detail the
+ * reference puts in its RuntimeError messages (H:630, :634, :649). */
+const char* bs_fp8_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BS_FP8_H */

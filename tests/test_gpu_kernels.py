@@ -1,0 +1,205 @@
+"""GPU parity of every kernel against the CPU oracle (seeded inputs, identical bytes on both sides).
+
+Bars:
+  * byte kernels (group quant, tile pack): bit-exact;
+  * bf16 GEMM outputs: max relative error <= 1e-2 against the fp32-accumulated oracle, with the
+    relative floor 1e-3 * max|ref| (logs/artifacts/20261031_hand/bench_hand.py:75 style);
+  * fused e4m3 outputs: at most 0.1% of elements differ, none by more than 1 e4m3 ulp;
+    group scales within 1e-6 relative.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GEMM_MAX_REL = 1e-2
+Q_ULP = 1
+Q_FRAC = 1e-3
+SCALE_REL = 1e-6
+
+
+def _ops():
+    from fp8_hand_b200 import ops
+    return ops
+
+
+def _dev(*ts):
+    return [t.cuda() for t in ts]
+
+
+# --------------------------------------------------------------------------- byte kernels
+@pytest.mark.parametrize("M,K", [(1, 128), (7, 512), (128, 5120), (301, 1024), (33, 17408)])
+def test_group_quant_bit_exact(cuda_lib, M, K):
+    x = O.make_activation(M, K, seed=M + K, outlier_frac=0.1)
+    x[0, :128] = 0
+    if M > 2:
+        x[1, 3] = 3.0e4
+        x[2] *= 1e-30
+    A, As = _ops().group_quant(x.cuda())
+    qr, sr = O.group_quant(x)
+    assert torch.equal(A.cpu().view(torch.uint8), qr.view(torch.uint8))
+    assert torch.equal(As.cpu(), sr)
+
+
+def test_group_quant_strided_rows(cuda_lib):
+    x = O.make_activation(16, 1024, seed=5)
+    big = torch.zeros(16, 1536, dtype=torch.bfloat16)
+    big[:, :1024] = x
+    A, As = _ops().group_quant(big.cuda()[:, :1024])
+    qr, sr = O.group_quant(x)
+    assert torch.equal(A.cpu().view(torch.uint8), qr.view(torch.uint8)) and torch.equal(As.cpu(), sr)
+
+
+@pytest.mark.parametrize("N,K", [(128, 128), (384, 640), (256, 5120)])
+def test_pack_tiles_bit_exact(cuda_lib, N, K):
+    g = torch.Generator().manual_seed(N * 7 + K)
+    w = torch.randint(0, 256, (N, K), dtype=torch.uint8, generator=g)
+    tiles = _ops().pack_tiles(w.cuda().view(torch.float8_e4m3fn))
+    assert torch.equal(tiles.cpu(), O.relayout_tiles(w))
+
+
+# --------------------------------------------------------------------------- GEMM
+GEMM_CASES = [
+    # (M, N, K)   decode (M <= 128) ...
+    (1, 256, 512),
+    (7, 384, 1024),
+    (16, 1024, 5120),
+    (33, 2048, 1024),
+    (5, 384, 17408),      # every tile spread over ~50 CTAs (many middle contributors)
+    (3, 128, 256),        # fewer units than SMs
+    (112, 1024, 5120),
+    (128, 6144, 5120),    # config 1
+    # ... prefill (M > 128)
+    (129, 512, 1024),
+    (200, 384, 640),      # odd number of 128-column blocks: half-empty last tile
+    (257, 2048, 5120),
+    (1024, 1024, 2048),
+]
+
+
+@pytest.mark.parametrize("tiled", [True, False])
+@pytest.mark.parametrize("M,N,K", GEMM_CASES)
+def test_gemm_bf16_matches_oracle(cuda_lib, M, N, K, tiled):
+    A, B, As, Bs, _ = O.make_gemm_case(M, N, K, seed=M * 31 + N + K, outlier_frac=0.05)
+    ops = _ops()
+    Bd = ops.pack_tiles(B.cuda()) if tiled else B.cuda()
+    C = ops.gemm(*_dev(A), Bd, *_dev(As, Bs), b_tiled=tiled)
+    torch.cuda.synchronize()
+    ref = O.blockwise_matmul(A, B, As, Bs)
+    assert C.dtype == torch.bfloat16 and tuple(C.shape) == (M, N)
+    assert O.max_rel_error(C.cpu(), ref) <= GEMM_MAX_REL
+    assert O.norm_rel_error(C.cpu(), ref) <= 4e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (300, 768, 2048), (128, 256, 17408)])
+def test_gemm_fp32_out_matches_oracle_tightly(cuda_lib, M, N, K):
+    A, B, As, Bs, _ = O.make_gemm_case(M, N, K, seed=N + K + M)
+    C = _ops().gemm(*_dev(A, B, As, Bs), out_dtype=torch.float32)
+    ref = O.blockwise_matmul(A, B, As, Bs)
+    assert C.dtype == torch.float32
+    # only fp32 summation order differs (tensor-core partials, split-K order)
+    assert O.norm_rel_error(C.cpu(), ref) <= 1e-5
+    assert O.max_rel_error(C.cpu(), ref) <= 1e-3
+
+
+@pytest.mark.parametrize("M", [2, 64, 500])
+def test_gemm_deterministic_and_linear(cuda_lib, M):
+    """Two launches give identical bytes; doubling As (exact in fp32) doubles C exactly."""
+    A, B, As, Bs, _ = O.make_gemm_case(M, 1024, 2048, seed=M)
+    ops = _ops()
+    Ad, Bd, Asd, Bsd = _dev(A, B, As, Bs)
+    C1 = ops.gemm(Ad, Bd, Asd, Bsd, out_dtype=torch.float32)
+    C2 = ops.gemm(Ad, Bd, Asd, Bsd, out_dtype=torch.float32)
+    C3 = ops.gemm(Ad, Bd, Asd * 2, Bsd, out_dtype=torch.float32)
+    assert torch.equal(C1, C2)
+    assert torch.equal(C3, C1 * 2)
+
+
+# --------------------------------------------------------------------------- fused gate_up
+def _check_fused(Q, Qs, A, B, As, Bs):
+    q_ref, s_ref, _ = O.fused_gate_up(A, B, As, Bs)
+    Q, Qs = Q.cpu(), Qs.cpu()
+    assert Q.dtype == torch.float8_e4m3fn and Qs.dtype == torch.float32
+    assert tuple(Q.shape) == tuple(q_ref.shape) and tuple(Qs.shape) == tuple(s_ref.shape)
+    rel = ((Qs - s_ref).abs() / s_ref).max().item()
+    ulp = O.e4m3_ulp_distance(Q, q_ref)
+    frac = (ulp > 0).float().mean().item()
+    assert rel <= SCALE_REL, f"scale rel err {rel:.3g}"
+    assert ulp.max().item() <= Q_ULP, f"max ulp {ulp.max().item()}"
+    assert frac <= Q_FRAC, f"{frac:.3%} of elements differ"
+
+
+FUSED_CASES = [(1, 512, 1024), (8, 2048, 5120), (14, 1024, 5120), (56, 512, 2048), (112, 2048, 5120),
+               (128, 256, 512), (129, 512, 1024), (300, 1024, 5120), (1024, 512, 1024)]
+
+
+@pytest.mark.parametrize("tiled", [True, False])
+@pytest.mark.parametrize("M,N2,K", FUSED_CASES)
+def test_fused_gate_up_matches_oracle(cuda_lib, M, N2, K, tiled):
+    A, B, As, Bs, _ = O.make_gemm_case(M, N2, K, seed=M + N2 + K, outlier_frac=0.01)
+    ops = _ops()
+    Bd = ops.pack_tiles(B.cuda()) if tiled else B.cuda()
+    Q, Qs = ops.gemm_silu_quant(*_dev(A), Bd, *_dev(As, Bs), b_tiled=tiled)
+    _check_fused(Q, Qs, A, B, As, Bs)
+
+
+def test_fused_gate_up_full_width_decode(cuda_lib):
+    """Config 2's real weight (2 x 17408 rows, K = 5120) at M = 112, checked on a block subset."""
+    M, inter, K = 112, 17408, 5120
+    x = O.make_activation(M, K, seed=77)
+    A, As = O.group_quant(x)
+    Bg, Bsg = O.make_weight(inter, K, seed=78)
+    Bu, Bsu = O.make_weight(inter, K, seed=79)
+    B = torch.cat([Bg.view(torch.uint8), Bu.view(torch.uint8)]).view(torch.float8_e4m3fn)
+    Bs = torch.cat([Bsg, Bsu])
+    Q, Qs = _ops().gemm_silu_quant(*_dev(A, B, As, Bs))
+    blocks = [0, 1, 67, 135]
+    rows_g = torch.cat([torch.arange(b * 128, (b + 1) * 128) for b in blocks])
+    sub_B = torch.cat([Bg.view(torch.uint8)[rows_g], Bu.view(torch.uint8)[rows_g]]).view(torch.float8_e4m3fn)
+    sub_Bs = torch.cat([Bsg[blocks], Bsu[blocks]])
+    cols = rows_g
+    _check_fused(Q.cpu()[:, cols], Qs.cpu()[:, blocks], A, sub_B, As, sub_Bs)
+
+
+# --------------------------------------------------------------------------- C-ABI contract
+def test_abi_rejects_bad_arguments(cuda_lib):
+    lib = cuda_lib
+    A, B, As, Bs, _ = O.make_gemm_case(4, 256, 256, seed=1)
+    Ad, Bd, Asd, Bsd = _dev(A, B, As, Bs)
+    C = torch.empty(4, 256, dtype=torch.bfloat16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    # K not a multiple of 128
+    assert lib.bs_fp8_gemm(Ad.data_ptr(), Bd.data_ptr(), C.data_ptr(), Asd.data_ptr(), Bsd.data_ptr(),
+                           4, 256, 200, 256, 0, 0, None, 0, s) == 1
+    # misaligned A
+    assert lib.bs_fp8_gemm(Ad.data_ptr() + 1, Bd.data_ptr(), C.data_ptr(), Asd.data_ptr(), Bsd.data_ptr(),
+                           4, 256, 256, 256, 0, 0, None, 0, s) == 2
+    # decode shape without workspace
+    assert lib.bs_fp8_gemm(Ad.data_ptr(), Bd.data_ptr(), C.data_ptr(), Asd.data_ptr(), Bsd.data_ptr(),
+                           4, 256, 256, 256, 0, 0, None, 0, s) == 3
+    # M == 0 is a no-op
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 0, 256, 256, 256, 0, 0, None, 0, s) == 0
+    # fused with N2 not a multiple of 256
+    Q = torch.empty(4, 64, dtype=torch.uint8, device="cuda")
+    assert lib.bs_fp8_gemm_silu_quant(Ad.data_ptr(), Bd.data_ptr(), Q.data_ptr(), Asd.data_ptr(), Bsd.data_ptr(),
+                                      Asd.data_ptr(), 4, 128, 256, 0, None, 0, s) == 1
+    assert lib.bs_fp8_workspace_bytes(4, 256, 256, 0) > 0
+    assert lib.bs_fp8_workspace_bytes(129, 256, 256, 0) == 0
+
+
+def test_bounded_wait_reports_timeout(cuda_lib):
+    """A wait that nothing satisfies gives up after its limit and leaves a status code; the
+    context stays usable afterwards."""
+    from fp8_hand_b200 import _native
+    assert _native.status(clear=True) == 0
+    rc = cuda_lib.bs_fp8_selftest_wait_timeout(ctypes.c_uint64(2_000_000), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert _native.status(clear=True) == 199
+    assert _native.status(clear=True) == 0
+    x = torch.ones(4, 128, dtype=torch.bfloat16, device="cuda")
+    A, As = _ops().group_quant(x)
+    assert torch.equal(As.cpu(), (torch.tensor(1.0) / torch.tensor(448.0)).expand(4, 1))

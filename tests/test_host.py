@@ -1,0 +1,182 @@
+"""CPU: the C-ABI library's surface and the host-side logic of the drop-in module (no GPU work)."""
+import ctypes
+import importlib
+import os
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "bs_fp8.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*[\w\s\*]+?\b(bs_fp8_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from fp8_hand_b200 import _build, _native
+    _build.build()
+    return _native.lib()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_functions()
+    assert len(names) >= 11
+    for name in names:
+        assert hasattr(lib, name), name
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(lib._name)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (bs_fp8_\w+)", nm))
+    assert set(names) <= exported
+
+
+def test_binding_covers_header():
+    from fp8_hand_b200 import _native
+    assert set(declared_functions()) == set(_native.SIGNATURES)
+
+
+def test_abi_version_and_error_strings(lib):
+    assert lib.bs_fp8_abi_version() == 1
+    for code in (0, 1, 2, 3, 4, 5, 6, 101, 102, 103, 104, 105, 199):
+        text = lib.bs_fp8_error_string(code).decode()
+        assert text and text != "unknown status code"
+    assert lib.bs_fp8_error_string(12345).decode() == "unknown status code"
+
+
+def test_argument_validation_needs_no_gpu(lib):
+    s = None
+    # K not a multiple of 128, N not a multiple of 128, ldc < N, bad dtype code: all rejected up front
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 200, 256, 0, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 200, 256, 256, 0, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 128, 0, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 7, None, 0, s) == 1
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 2, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm_silu_quant(None, None, None, None, None, None, 4, 384, 256, 0, None, 0, s) == 1
+    # M == 0 is a no-op that touches nothing
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 0, 256, 256, 256, 0, 0, None, 0, s) == 0
+    assert lib.bs_fp8_group_quant(None, 256, None, None, 0, 256, s) == 0
+    assert lib.bs_fp8_group_quant(None, 256, None, None, 4, 200, s) == 1
+    assert lib.bs_fp8_pack_tiles(None, None, 100, 128, s) == 1
+    # null pointers with a real shape
+    assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
+
+
+def test_workspace_size_formula(lib):
+    # decode shapes need counters + G * 2 * nwg * ntp * 128 floats; prefill shapes need none
+    assert lib.bs_fp8_workspace_bytes(129, 256, 256, 0) == 0
+    assert lib.bs_fp8_workspace_bytes(0, 256, 256, 0) == 0
+    w1 = lib.bs_fp8_workspace_bytes(1, 34816, 5120, 1)
+    w112 = lib.bs_fp8_workspace_bytes(112, 34816, 5120, 1)
+    assert 0 < w1 < w112
+    sms = lib.bs_fp8_num_sms() or 148
+    assert w112 == 256 + sms * 2 * 2 * 112 * 128 * 4 + (136 * 4 + 255) // 256 * 256 - 256
+
+
+def _fresh_module(monkeypatch, **env):
+    for k in ("SGLANG_FP8_HAND_GEMM", "SGLANG_FP8_HAND_FUSED", "SGLANG_FP8_HAND_FUSED_MIN_M"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    import fp8_hand_b200.fp8_hand_sm100 as m
+    return importlib.reload(m)
+
+
+def test_env_switch_semantics(monkeypatch):
+    m = _fresh_module(monkeypatch)
+    assert (m.ENABLED, m.FUSED_ENABLED, m.FUSED_MIN_M) == (False, False, 1)
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1")
+    assert (m.ENABLED, m.FUSED_ENABLED) == (True, True)
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1", SGLANG_FP8_HAND_FUSED="0")
+    assert (m.ENABLED, m.FUSED_ENABLED) == (True, False)
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1", SGLANG_FP8_HAND_FUSED_MIN_M="1024")
+    assert m.FUSED_MIN_M == 1024
+    _fresh_module(monkeypatch)
+
+
+def test_select_tiles():
+    from fp8_hand_b200 import select
+    assert select(34816, 1)["kind"] == "decode" and select(34816, 1)["NTP"] == 16
+    assert select(34816, 112)["NTP"] == 112
+    assert select(6144, 128)["kind"] == "decode"
+    p = select(34816, 129)
+    assert p["kind"] == "prefill" and (p["BM"], p["BN"]) == (128, 256)
+
+
+class _Proj(torch.nn.Module):
+    def __init__(self, n, k, tiles=True):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.empty(n, k, dtype=torch.float8_e4m3fn, device="meta"),
+                                         requires_grad=False)
+        if tiles:
+            self.weight.tiles = torch.empty(n // 128, k // 128, 128, 128, dtype=torch.uint8)
+        self.weight_scale_inv = torch.nn.Parameter(torch.ones(n // 128, k // 128), requires_grad=False)
+        self.bias = None
+
+
+def test_dropin_fallback_contract(monkeypatch):
+    """matmul -> False without tiles; fused_gate_up -> None when disabled, too small or ineligible.
+    None of these reach the GPU."""
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1", SGLANG_FP8_HAND_FUSED_MIN_M="64")
+    x = torch.zeros(8, 256, dtype=torch.bfloat16)
+    assert m.fused_gate_up(_Proj(512, 256), x) is None                  # M < FUSED_MIN_M
+    assert m.fused_gate_up(_Proj(512, 256, tiles=False), torch.zeros(64, 256, dtype=torch.bfloat16)) is None
+    assert m.fused_gate_up(_Proj(384, 256), torch.zeros(64, 256, dtype=torch.bfloat16)) is None  # N % 256
+    assert m.fused_gate_up(_Proj(512, 256), torch.zeros(64, 256)) is None  # not bf16
+    w = torch.empty(256, 256, dtype=torch.float8_e4m3fn)
+    assert m.matmul(None, w, None, None, None, 8, 256, 256, [128, 128]) is False
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1", SGLANG_FP8_HAND_FUSED="0")
+    assert m.fused_gate_up(_Proj(512, 256), torch.zeros(4096, 256, dtype=torch.bfloat16)) is None
+    _fresh_module(monkeypatch)
+
+
+def test_relayout_is_noop_off_b200(monkeypatch):
+    m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1")
+    model = torch.nn.Module()
+    model.proj = torch.nn.Linear(128, 128, bias=False)
+    model.proj.weight = torch.nn.Parameter(torch.zeros(128, 128).to(torch.float8_e4m3fn), requires_grad=False)
+    model.proj.weight_scale_inv = torch.nn.Parameter(torch.ones(1, 1), requires_grad=False)
+    before = model.proj.weight
+    m.relayout(model)   # no B200 here: nothing changes
+    assert model.proj.weight is before and getattr(model.proj.weight, "tiles", None) is None
+    _fresh_module(monkeypatch)
+
+
+def test_eligibility_rules():
+    from fp8_hand_b200 import fp8_hand_sm100 as m
+    w = torch.empty(256, 384, dtype=torch.float8_e4m3fn)
+    s = torch.ones(2, 3)
+    assert m.eligible("layers.0.mlp.gate_up_proj", w, s)
+    assert not m.eligible("lm_head", w, s)
+    assert not m.eligible("x", w, torch.ones(2, 2))
+    assert not m.eligible("x", torch.empty(256, 384, dtype=torch.bfloat16), s)
+    assert not m.eligible("x", torch.empty(200, 384, dtype=torch.float8_e4m3fn), torch.ones(1, 3))
+
+
+def test_ops_refuse_cpu_tensors():
+    """No CPU fallback: the product path rejects host tensors loudly."""
+    from fp8_hand_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.group_quant(torch.zeros(4, 128, dtype=torch.bfloat16))
+    A = torch.zeros(4, 128, dtype=torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gemm(A, torch.zeros(128, 128, dtype=torch.float8_e4m3fn), torch.ones(4, 1), torch.ones(1, 1))
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    from fp8_hand_b200 import _native
+    monkeypatch.setattr(_native, "_LIB", None)
+    monkeypatch.setattr(_native, "library_path", lambda: tmp_path / "absent.so")
+    with pytest.raises(RuntimeError, match="no CPU or Triton fallback"):
+        _native.lib()
+
+
+def test_build_command_targets_sm100a():
+    from fp8_hand_b200 import _build
+    flags = " ".join(_build.NVCC_FLAGS)
+    assert "arch=compute_100a,code=sm_100a" in flags and "-lineinfo" in flags

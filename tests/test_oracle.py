@@ -1,0 +1,98 @@
+"""CPU: the oracle against the golden outputs of the reference's own functions."""
+import hashlib
+
+import numpy as np
+import torch
+
+from oracle import oracle as O
+
+
+def _bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits)).view(torch.bfloat16)
+
+
+def _e4m3(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits)).view(torch.float8_e4m3fn)
+
+
+def test_activation_quant_matches_reference_bytes(golden):
+    g, _ = golden
+    x = _bf16(g["act_x_bf16_bits"])
+    q, s = O.group_quant(x)
+    assert np.array_equal(q.view(torch.uint8).numpy(), g["act_q_bits"])
+    assert np.array_equal(s.numpy(), g["act_scale"])
+
+
+def test_activation_quant_edge_rows(golden):
+    g, _ = golden
+    s = g["act_scale"]
+    assert np.all(s[1] == np.float32(1e-12))          # all-zero row: clamped scale, zero bytes
+    assert np.all(g["act_q_bits"][1] == 0)
+    assert np.all(s[3] == np.float32(1e-12))          # tiny row below the clamp
+    assert np.isclose(s[4, 0], 3.0e4 / 448, rtol=1e-2)  # large values (bf16-rounded 3e4)
+    assert np.all(np.isfinite(_e4m3(g["act_q_bits"]).float().numpy()))
+
+
+def test_weight_quant_matches_reference_bytes(golden):
+    g, _ = golden
+    w = _bf16(g["w_bf16_bits"])
+    q, s = O.weight_quant(w)
+    assert np.array_equal(q.view(torch.uint8).numpy(), g["w_q_bits"])
+    assert np.array_equal(s.numpy(), g["w_scale"])
+
+
+def test_ref_matmul_matches_reference(golden):
+    g, _ = golden
+    A, B = _e4m3(g["act_q_bits"]), _e4m3(g["w_q_bits"])
+    As, Bs = torch.from_numpy(g["act_scale"]), torch.from_numpy(g["w_scale"])
+    C = O.ref_matmul(A, B, As, Bs)
+    assert np.allclose(C.numpy(), g["gemm_ref_out"], rtol=1e-6, atol=1e-6)
+
+
+def test_blockwise_matmul_tracks_reference_oracle(golden):
+    g, _ = golden
+    A, B = _e4m3(g["act_q_bits"]), _e4m3(g["w_q_bits"])
+    As, Bs = torch.from_numpy(g["act_scale"]), torch.from_numpy(g["w_scale"])
+    C = torch.from_numpy(g["gemm_ref_out"])
+    Cb = O.blockwise_matmul(A, B, As, Bs)
+    # same math, different fp32 summation order
+    assert O.norm_rel_error(Cb, C) < 1e-5
+    assert O.max_rel_error(Cb, C) < 1e-3
+
+
+def test_relayout_matches_reference_module(golden):
+    g, meta = golden
+    for name, entry in meta["relayout"].items():
+        n, k = entry["shape"]
+        rng = np.random.default_rng(entry["seed"])
+        raw = torch.from_numpy(rng.integers(0, 256, size=(n, k), dtype=np.uint8))
+        tiles = O.relayout_tiles(raw).numpy()
+        if entry["moved"]:
+            assert list(tiles.shape) == entry["tiles_shape"]
+            assert hashlib.sha256(tiles.tobytes()).hexdigest() == entry["tiles_sha256"]
+            assert np.array_equal(tiles[0, 0], g[f"relayout_{name}_first_tile"])
+            assert np.array_equal(tiles[-1, -1], g[f"relayout_{name}_last_tile"])
+    assert meta["relayout"]["lm_head"]["moved"] is False
+
+
+def test_fused_oracle_matches_chain_statistics():
+    """The fused restatement against the unfused chain it replaces: same dequant error level and
+    group scales within ~1.3e-2 (the reference measured 0.0216 vs 0.0213 and 1.1-1.25e-2,
+    logs/artifacts/20261031_hand/C/logs/fused1.txt:3-8)."""
+    A, B, As, Bs, _ = O.make_gemm_case(64, 512, 1024, seed=3)
+    q, s, y = O.fused_gate_up(A, B, As, Bs)
+    qc, sc, yc = O.chain_gate_up(A, B, As, Bs)
+    deq = q.float() * s.repeat_interleave(128, -1)
+    err_fused = ((deq - y).abs().mean() / y.abs().mean()).item()
+    deqc = qc.float() * sc.repeat_interleave(128, -1)
+    err_chain = ((deqc - y).abs().mean() / y.abs().mean()).item()
+    assert 0.015 < err_fused < 0.03 and 0.015 < err_chain < 0.03
+    assert ((s - sc).abs() / s).max().item() < 2e-2
+    assert torch.isfinite(deq).all()
+
+
+def test_e4m3_ulp_distance():
+    a = torch.tensor([0.0, 1.0, -1.0, 448.0, 2.0]).to(torch.float8_e4m3fn)
+    b = torch.tensor([0.0, 1.125, -1.125, 416.0, -2.0]).to(torch.float8_e4m3fn)
+    d = O.e4m3_ulp_distance(a, b).tolist()
+    assert d[:4] == [0, 1, 1, 1] and d[4] > 1

@@ -1,0 +1,358 @@
+// C-ABI entry points of libbs_fp8_sm100.so: argument checks, TMA descriptor creation, kernel
+// selection and launch. One translation unit so that every kernel can name the status word.
+#include <mutex>
+#include <cstdio>
+#include <cstring>
+
+#include <cudaTypedefs.h>
+
+#include "bs_common.cuh"
+#include "bs_prefill.cuh"
+#include "bs_decode.cuh"
+#include "bs_quant.cuh"
+#include "../../include/bs_fp8.h"
+
+// Library status word: kernels record the first bounded-wait timeout here.
+__device__ int g_bs_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Text of the last CUDA runtime failure seen by this library on the calling thread.
+thread_local char g_last_cuda_error[256] = "";
+
+int cuda_fail(cudaError_t e, const char* where) {
+  std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s (%s)", where, cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return BS_ERR_CUDA;
+}
+
+// Launch result: the launch's own error, not an older one left in the runtime's error slot.
+int launch_status(const char* where) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BS_OK : cuda_fail(e, where);
+}
+
+struct DeviceState {
+  std::once_flag once;
+  int num_sms = 0;
+  int* status = nullptr;
+  int err = 0;
+};
+DeviceState g_dev[kMaxDevices];
+
+std::once_flag g_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+// Per-device set-up (SM count, status word address), done once per device with that device current.
+DeviceState* device_state() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  DeviceState* d = &g_dev[dev];
+  std::call_once(d->once, [d, dev] {
+    cudaError_t e = cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) d->err = cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+    void* sym = nullptr;
+    e = cudaGetSymbolAddress(&sym, g_bs_status);
+    if (e != cudaSuccess) d->err = cuda_fail(e, "cudaGetSymbolAddress(status word)");
+    d->status = static_cast<int*>(sym);
+  });
+  return d->err ? nullptr : d;
+}
+
+// 2-D uint8 tensor map with a 128-byte-swizzled box; out-of-range elements read as zero.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+             uint32_t box_outer) {
+  auto enc = encoder();
+  if (!enc) return BS_ERR_TMAP;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BS_OK : BS_ERR_TMAP;
+}
+
+// Weight map: tile-first [N*K/128 rows of 128 bytes] or row-major [N rows of K bytes].
+int make_weight_map(CUtensorMap* m, const void* B, int N, int K, int tiled) {
+  if (tiled)
+    return make_map(m, B, 128, static_cast<uint64_t>(N) * (K / 128), 128, 128, 128);
+  return make_map(m, B, K, N, K, 128, 128);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int ntp_for(int M) { return ((M + 15) / 16) * 16; }
+
+// Grid of the decode kernels: one CTA per SM, never more CTAs than (tile, K block) units.
+int decode_grid(int num_sms, int tiles, int KB) {
+  const long long units = static_cast<long long>(tiles) * KB;
+  return static_cast<int>(units < num_sms ? units : num_sms);
+}
+
+size_t decode_ws_bytes(int G, int nwg, int ntp, int tiles) {
+  const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
+  return counters + static_cast<size_t>(G) * 2 * nwg * ntp * 128 * sizeof(float);
+}
+
+// One-time per (kernel, device) preparation: opt in to the kernel's dynamic shared memory and,
+// for kernels that move registers between warpgroups with setmaxnreg, check that the build gave
+// them exactly the launch register count the split was computed for. The state is keyed on the
+// kernel itself (a template value parameter), since all GEMM kernels share one signature.
+template <auto kernel>
+int prepare_kernel(int smem_bytes, bool split_regs) {
+  struct State {
+    std::once_flag once[kMaxDevices];
+    int rc[kMaxDevices];
+  };
+  static State st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BS_ERR_CUDA;
+  std::call_once(st.once[dev], [&] {
+    int rc = BS_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) rc = cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+    if (rc == BS_OK && split_regs) {
+      cudaFuncAttributes attr;
+      e = cudaFuncGetAttributes(&attr, kernel);
+      if (e != cudaSuccess)
+        rc = cuda_fail(e, "cudaFuncGetAttributes");
+      else if (attr.numRegs != bs::kLaunchRegs)
+        rc = BS_ERR_BUILD;
+    }
+    st.rc[dev] = rc;
+  });
+  return st.rc[dev];
+}
+
+template <bool FUSED, int NTP>
+int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const bs::GemmParams& p, int grid,
+                  cudaStream_t s) {
+  using Cfg = bs::DecodeCfg<FUSED, NTP>;
+  constexpr auto kern = bs::k_decode<FUSED, NTP>;
+  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::kSplitRegs);
+  if (rc != BS_OK) return rc;
+  cudaGetLastError();  // clear an older error so the check below sees this launch only
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmW, tmX, p);
+  return launch_status("k_decode launch");
+}
+
+template <bool FUSED>
+int dispatch_decode(int ntp, const CUtensorMap& tmW, const CUtensorMap& tmX, const bs::GemmParams& p, int grid,
+                    cudaStream_t s) {
+  switch (ntp) {
+    case 16: return launch_decode<FUSED, 16>(tmW, tmX, p, grid, s);
+    case 32: return launch_decode<FUSED, 32>(tmW, tmX, p, grid, s);
+    case 48: return launch_decode<FUSED, 48>(tmW, tmX, p, grid, s);
+    case 64: return launch_decode<FUSED, 64>(tmW, tmX, p, grid, s);
+    case 80: return launch_decode<FUSED, 80>(tmW, tmX, p, grid, s);
+    case 96: return launch_decode<FUSED, 96>(tmW, tmX, p, grid, s);
+    case 112: return launch_decode<FUSED, 112>(tmW, tmX, p, grid, s);
+    case 128: return launch_decode<FUSED, 128>(tmW, tmX, p, grid, s);
+    default: return BS_ERR_ARG;
+  }
+}
+
+template <bool FUSED>
+int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::GemmParams& p, int num_tiles,
+                   int num_sms, cudaStream_t s) {
+  using Cfg = bs::PrefillCfg<FUSED>;
+  constexpr auto kern = bs::k_prefill<FUSED>;
+  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, true);
+  if (rc != BS_OK) return rc;
+  const int grid = num_tiles < num_sms ? num_tiles : num_sms;
+  cudaGetLastError();
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmA, tmB, p);
+  return launch_status("k_prefill launch");
+}
+
+// Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant.
+int run_gemm(bool fused, const void* A, const void* B, void* out, const float* As, const float* Bs, float* qs,
+             int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0) return BS_ERR_ARG;
+  if (fused && N % 256 != 0) return BS_ERR_ARG;
+  if (!fused && (ldc < N || ldc % 8 != 0 || (out_dtype != 0 && out_dtype != 1))) return BS_ERR_ARG;
+  if (b_tiled != 0 && b_tiled != 1) return BS_ERR_ARG;
+  if (M == 0) return BS_OK;
+  if (!A || !B || !out || !As || !Bs || (fused && !qs)) return BS_ERR_ARG;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(out)) return BS_ERR_ALIGN;
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  bs::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.KB = K / 128;
+  p.ldc = fused ? N / 2 : ldc;
+  p.b_tiled = b_tiled;
+  p.out_f32 = fused ? 0 : out_dtype;
+  p.group_m = 16;
+  p.As = As;
+  p.Bs = Bs;
+  p.out = out;
+  p.qs = qs;
+  p.status = d->status;
+
+  CUtensorMap tmB;
+  if (make_weight_map(&tmB, B, N, K, b_tiled) != BS_OK) return BS_ERR_TMAP;
+
+  if (M <= 128) {
+    const int ntp = ntp_for(M);
+    const int nwg = fused ? 2 : 1;
+    const int tiles = fused ? N / 256 : N / 128;
+    const int grid = decode_grid(d->num_sms, tiles, K / 128);
+    const size_t need = decode_ws_bytes(grid, nwg, ntp, tiles);
+    if (!ws || ws_bytes < need || !aligned16(ws)) return BS_ERR_WORKSPACE;
+    const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
+    p.cnt = static_cast<int*>(ws);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + counters);
+    CUtensorMap tmX;
+    if (make_map(&tmX, A, K, M, K, 128, ntp) != BS_OK) return BS_ERR_TMAP;
+    return fused ? dispatch_decode<true>(ntp, tmB, tmX, p, grid, s) : dispatch_decode<false>(ntp, tmB, tmX, p, grid, s);
+  }
+
+  CUtensorMap tmA;
+  if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
+  const int num_m = (M + 127) / 128;
+  const int num_n = fused ? N / 256 : (N / 128 + 1) / 2;
+  return fused ? launch_prefill<true>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
+               : launch_prefill<false>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
+}
+
+__global__ void k_selftest_wait(uint64_t limit_ns, int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    bs::mbar_init(&bar, 1);
+    abort_flag = 0;
+    bs::fence_mbar_init();
+  }
+  __syncthreads();
+  // Nothing ever arrives on `bar`: the wait must give up after limit_ns.
+  if (threadIdx.x == 0) bs::mbar_wait(&bar, 0, &abort_flag, status, bs::kErrTimeoutSelftest, limit_ns);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bs_fp8_gemm(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
+                int ldc, int b_tiled, int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype, workspace, workspace_bytes,
+                  stream);
+}
+
+int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* As, const float* Bs, float* Qs,
+                           int M, int N2, int K, int b_tiled, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  return run_gemm(true, A, B, Q, As, Bs, Qs, M, N2, K, N2 / 2, b_tiled, 0, workspace, workspace_bytes, stream);
+}
+
+size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {
+  if (M <= 0 || M > 128 || N <= 0 || K <= 0 || K % 128 || N % (fused ? 256 : 128)) return 0;
+  DeviceState* d = device_state();
+  const int sms = d ? d->num_sms : 148;
+  const int tiles = fused ? N / 256 : N / 128;
+  return decode_ws_bytes(decode_grid(sms, tiles, K / 128), fused ? 2 : 1, ntp_for(M), tiles);
+}
+
+int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0 || ldx < K || ldx % 8 != 0) return BS_ERR_ARG;
+  if (M == 0) return BS_OK;
+  if (!x || !A || !As) return BS_ERR_ARG;
+  if (!aligned16(x) || !aligned16(A)) return BS_ERR_ALIGN;
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  const long long groups = static_cast<long long>(M) * (K / 128);
+  const int per_block = bs::kQuantThreads / 16;
+  long long blocks = (groups + per_block - 1) / per_block;
+  const long long cap = static_cast<long long>(d->num_sms) * 16;
+  if (blocks > cap) blocks = cap;
+  cudaGetLastError();
+  bs::k_group_quant<<<static_cast<int>(blocks), bs::kQuantThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<uint8_t*>(A), As, M, K);
+  return launch_status("k_group_quant launch");
+}
+
+int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return BS_ERR_ARG;
+  if (!W || !tiles) return BS_ERR_ARG;
+  if (!aligned16(W) || !aligned16(tiles)) return BS_ERR_ALIGN;
+  const long long nt = static_cast<long long>(N / 128) * (K / 128);
+  if (nt > 0x7fffffffLL) return BS_ERR_ARG;
+  cudaGetLastError();
+  bs::k_pack_tiles<<<static_cast<int>(nt), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(W), static_cast<uint8_t*>(tiles), N, K);
+  return launch_status("k_pack_tiles launch");
+}
+
+int bs_fp8_status(int* code, int clear) {
+  if (!code) return BS_ERR_ARG;
+  if (!device_state()) return BS_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BS_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_bs_status, sizeof(int)) != cudaSuccess) return BS_ERR_CUDA;
+  *code = v;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_bs_status, &zero, sizeof(int)) != cudaSuccess) return BS_ERR_CUDA;
+  }
+  return BS_OK;
+}
+
+int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  if (limit_ns > 10000000000ull) return BS_ERR_ARG;  // keep the self-test short
+  cudaGetLastError();
+  k_selftest_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, d->status);
+  return launch_status("k_selftest_wait launch");
+}
+
+int bs_fp8_num_sms(void) {
+  DeviceState* d = device_state();
+  return d ? d->num_sms : 0;
+}
+
+const char* bs_fp8_error_string(int code) {
+  switch (code) {
+    case BS_OK: return "ok";
+    case BS_ERR_ARG: return "argument outside the contract (shape, stride or dtype)";
+    case BS_ERR_ALIGN: return "pointer or row stride not 16-byte aligned";
+    case BS_ERR_WORKSPACE: return "workspace missing or too small";
+    case BS_ERR_TMAP: return "TMA descriptor could not be created";
+    case BS_ERR_CUDA: return "CUDA runtime call failed";
+    case BS_ERR_BUILD: return "kernel register count does not match its setmaxnreg split; refusing to launch";
+    case BS_ERR_TIMEOUT_FULL: return "device: bounded wait for a TMA stage ran out";
+    case BS_ERR_TIMEOUT_EMPTY: return "device: bounded wait for a free stage ran out";
+    case BS_ERR_TIMEOUT_PFULL: return "device: bounded wait for an MMA partial ran out";
+    case BS_ERR_TIMEOUT_PEMPTY: return "device: bounded wait for a TMEM buffer ran out";
+    case BS_ERR_TIMEOUT_DRAIN: return "device: teardown drain ran out";
+    case BS_ERR_TIMEOUT_SELFTEST: return "device: self-test wait ran out (expected)";
+    default: return "unknown status code";
+  }
+}
+
+int bs_fp8_abi_version(void) { return 1; }
+
+const char* bs_fp8_last_cuda_error(void) { return g_last_cuda_error; }
+
+}  // extern "C"

@@ -1,0 +1,351 @@
+// Prefill-size block-scaled FP8 GEMM for sm_100a (M > 128 rows).
+//
+// Computes, per output tile of 128 rows x 256 columns,
+//     C[m, n] = sum_kb  P_kb[m, n] * (As[m, kb] * Bs[n / 128, kb])
+// where P_kb is the fp32 product of one 128-wide K block of e4m3 activations and e4m3 weights.
+// This is the arithmetic of the reference kernel (patches/fp8_hand_sm89.py:189-199 and
+// :275-280): one fp32 partial per 128-K block, the scale product a_s * b_s rounded once, then
+// C = fma(partial, scale, C). The reference keeps the partial in mma.sync registers; here it
+// comes from tcgen05.mma into TMEM and is promoted by CUDA-core warps.
+//
+// CTA layout (384 threads, one persistent CTA per SM):
+//   warps 0-7  promotion + epilogue. Warp w reads TMEM lanes 32*(w%4)..+31 (one tile row per
+//              thread) and columns 128*(w/4)..+127, i.e. exactly one 128-wide weight block, so
+//              the scale product is one scalar per thread per K block.
+//   warp 8     TMA producer: A box 128x128 and two weight boxes 128x128 per K block.
+//   warp 9     TMEM allocator + MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32) per K block
+//              into one of two TMEM partial buffers (2 x 256 columns = all 512).
+//   warps 10-11 idle; warps 8-11 form the warpgroup that hands its registers to warps 0-7
+//              (setmaxnreg 40 / 232), since each promotion thread keeps 128 fp32 accumulators.
+// The partial buffers are double-buffered, so the tensor core computes block kb+1 while the
+// promotion warps fold block kb into their register accumulators.
+//
+// FUSED=true is the gate_up + SiLU*up + per-token-group quant kernel (reference
+// patches/fp8_hand_sm89.py:314-583): the 256 MMA columns are gate block j and up block
+// j + I/128 (I = N/2), the up accumulators cross to the gate warps through shared memory, and
+// each gate thread owns a whole 128-wide quant group of its row:
+//   y = silu(g) * u;  scale = max(amax|y|, 1e-10) / 448;  q = sat_e4m3(y * (1 / scale)).
+#pragma once
+#include "bs_common.cuh"
+
+namespace bs {
+
+struct GemmParams {
+  int M, N, K, KB;   // N: output features (plain) or gate+up rows, 2*I (fused)
+  int ldc;           // plain: row stride of the output, in elements
+  int b_tiled;       // 1: weights in tile-first layout [N/128][K/128][128][128]; 0: row-major [N, K]
+  int out_f32;       // plain: write fp32 instead of bf16
+  int group_m;       // prefill raster: M tiles per group
+  const float* As;   // [M, KB] activation group scales
+  const float* Bs;   // [N/128, KB] weight block scales
+  void* out;         // plain: C [M, ldc]; fused: Q e4m3 [M, I]
+  float* qs;         // fused: Qs [M, I/128]
+  float* ws;         // decode split-K partials
+  int* cnt;          // decode split-K arrival counters, one per tile, zero between launches
+  int* status;       // library status word
+};
+
+template <bool FUSED>
+struct PrefillCfg {
+  static constexpr int kThreads = 384;
+  static constexpr int kStages = FUSED ? 3 : 4;
+  static constexpr int kABytes = 128 * 128;
+  static constexpr int kBBytes = 256 * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 : 0;
+  static constexpr int kBarOff = kStages * kStageBytes + kXchBytes;
+  static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers, then slack for 1 KB alignment
+  static constexpr int kTmemCols = 512;
+};
+
+// Tile index -> (m tile, n tile), grouped so that CTAs running together share A and B tiles in L2.
+__device__ __forceinline__ void prefill_tile_coords(int tile, int num_m, int num_n, int group_m, int& tm,
+                                                    int& tn) {
+  const int per_group = group_m * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * group_m;
+  const int gm = min(num_m - first_m, group_m);
+  const int in = tile - g * per_group;
+  tm = first_m + in % gm;
+  tn = in / gm;
+}
+
+// Weight box for (128-row block nb, K block kb) in either supported layout.
+__device__ __forceinline__ void load_weight_box(void* dst, const CUtensorMap* map, uint64_t* bar, int nb, int kb,
+                                                int KB, int tiled, uint64_t policy) {
+  if (tiled)
+    tma_load_2d(dst, map, bar, 0, (nb * KB + kb) * 128, policy);
+  else
+    tma_load_2d(dst, map, bar, kb * 128, nb * 128, policy);
+}
+
+template <bool FUSED>
+__global__ void __launch_bounds__(384, 1)
+    k_prefill(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const GemmParams p) {
+  using Cfg = PrefillCfg<FUSED>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* full = bars;              // [S]   TMA -> MMA
+  uint64_t* empty = bars + S;         // [S]   MMA -> TMA
+  uint64_t* pfull = bars + 2 * S;     // [2]   MMA -> promotion
+  uint64_t* pempty = bars + 2 * S + 2;  // [2] promotion -> MMA
+  uint64_t* drain = bars + 2 * S + 4;   // [1] MMA teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xch = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&pfull[i], 1);
+      mbar_init(&pempty[i], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int M = p.M, KB = p.KB;
+  const int nblk = p.N / 128;                       // 128-row weight blocks
+  const int I_blk = FUSED ? nblk / 2 : 0;           // fused: gate blocks (= up blocks)
+  const int num_m = (M + 127) / 128;
+  const int num_n = FUSED ? I_blk : (nblk + 1) / 2;
+  const int num_tiles = num_m * num_n;
+
+  // Each role changes its register budget at the top of its own branch: code after a merge of
+  // the two branches must fit the smaller budget, and only the short teardown follows one.
+  if (warp >= 8) {
+    regs_decrease<kProducerRegs>();
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
+      int s = 0;
+      uint32_t ph = 0, issued = 0, parity_bits = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int tm, tn;
+        prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
+        const int nb0 = FUSED ? tn : 2 * tn;
+        const int nb1 = FUSED ? tn + I_blk : 2 * tn + 1;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * Cfg::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          tma_load_2d(st, &tmA, &full[s], kb * 128, tm * 128, pol_a);
+          load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
+          load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
+          issued |= 1u << s;
+          parity_bits = (parity_bits & ~(1u << s)) | (ph << s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Leave no copy in flight: wait (bounded) for the last fill of every stage.
+        for (int i = 0; i < S; ++i)
+          if (issued & (1u << i))
+            mbar_wait(&full[i], (parity_bits >> i) & 1u, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+      int s = 0, b = 0;
+      uint32_t ph = 0, pph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull) ||
+              !mbar_wait(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t b0 = a0 + Cfg::kABytes;
+          const uint32_t d = tmem + static_cast<uint32_t>(b * 256);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_e4m3(d, desc_kmajor_sw128(a0 + 32 * k), desc_kmajor_sw128(b0 + 32 * k), idesc, k > 0 ? 1u : 0u);
+          mma_commit(&empty[s]);
+          mma_commit(&pfull[b]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+          if (++b == 2) {
+            b = 0;
+            pph ^= 1;
+          }
+        }
+      }
+      // Every MMA issued so far completes before TMEM is released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
+    }
+  }
+  } else {
+    regs_increase<kConsumerRegs>();
+    // ------------------------------------------------------------ promotion + epilogue
+    const int wg = warp >> 2;         // 0: columns 0-127 of the tile, 1: columns 128-255
+    const int q = warp & 3;           // TMEM lane quarter
+    const int r = q * 32 + lane;      // row inside the tile
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    // After an abort these warps keep walking the tile loop (skipping every wait, TMEM read and
+    // store) so that both warpgroups still meet at the same named barriers.
+    int b = 0;
+    uint32_t pph = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
+      const int row = tm * 128 + r;
+      const bool row_ok = row < M;
+      const int nb = FUSED ? (wg == 0 ? tn : tn + I_blk) : 2 * tn + wg;
+      const bool col_ok = nb < nblk;
+      const float* as_row = p.As + static_cast<size_t>(row_ok ? row : 0) * KB;
+      const float* bs_row = p.Bs + static_cast<size_t>(col_ok ? nb : 0) * KB;
+
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+
+      // Scale prefetch two K blocks ahead (L2 latency is about one K block of MMA time).
+      float a_n0 = row_ok ? ldg_f32(as_row) : 0.f, b_n0 = col_ok ? ldg_f32(bs_row) : 0.f;
+      float a_n1 = (row_ok && KB > 1) ? ldg_f32(as_row + 1) : 0.f;
+      float b_n1 = (col_ok && KB > 1) ? ldg_f32(bs_row + 1) : 0.f;
+
+      for (int kb = 0; kb < KB; ++kb) {
+        const float sa = a_n0, sb = b_n0;
+        a_n0 = a_n1;
+        b_n0 = b_n1;
+        if (kb + 2 < KB) {
+          a_n1 = row_ok ? ldg_f32(as_row + kb + 2) : 0.f;
+          b_n1 = col_ok ? ldg_f32(bs_row + kb + 2) : 0.f;
+        }
+        const float sc = __fmul_rn(sa, sb);
+        if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * 256 + wg * 128);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(v[i]), sc, acc[c * 32 + i]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[b]);
+        }
+        if (++b == 2) {
+          b = 0;
+          pph ^= 1;
+        }
+      }
+
+      if constexpr (!FUSED) {
+        if (ok && row_ok && col_ok) {
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(row) * p.ldc +
+                                                    static_cast<size_t>(nb) * 128);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
+                                                  static_cast<size_t>(row) * p.ldc + static_cast<size_t>(nb) * 128);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              dst[j] = make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
+                                  pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]),
+                                  pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+          }
+        }
+      } else {
+        // Up accumulators cross to the gate warps. 16-byte chunks are XOR-swizzled by row so
+        // that the 8 rows of one store phase hit 8 different bank groups.
+        float4* x4 = reinterpret_cast<float4*>(xch);
+        if (wg == 1) {
+#pragma unroll
+          for (int c4 = 0; c4 < 32; ++c4)
+            x4[r * 32 + (c4 ^ (r & 7))] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+        }
+        named_bar_sync(1, 256);
+        if (wg == 0) {
+          float amax = 0.f;
+#pragma unroll
+          for (int c4 = 0; c4 < 32; ++c4) {
+            const float4 u = x4[r * 32 + (c4 ^ (r & 7))];
+            acc[4 * c4 + 0] = silu_mul(acc[4 * c4 + 0], u.x);
+            acc[4 * c4 + 1] = silu_mul(acc[4 * c4 + 1], u.y);
+            acc[4 * c4 + 2] = silu_mul(acc[4 * c4 + 2], u.z);
+            acc[4 * c4 + 3] = silu_mul(acc[4 * c4 + 3], u.w);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(acc[4 * c4]), fabsf(acc[4 * c4 + 1])),
+                                     fmaxf(fabsf(acc[4 * c4 + 2]), fabsf(acc[4 * c4 + 3]))));
+          }
+          const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
+          const float inv = __fdiv_rn(1.0f, scale);
+          if (ok && row_ok) {
+            const int I = I_blk * 128;
+            p.qs[static_cast<size_t>(row) * I_blk + tn] = scale;
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * I +
+                                                  static_cast<size_t>(tn) * 128);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint32_t w[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const int e = 16 * j + 4 * h;
+                w[h] = f2_to_e4m3x2(__fmul_rn(acc[e], inv), __fmul_rn(acc[e + 1], inv)) |
+                       (f2_to_e4m3x2(__fmul_rn(acc[e + 2], inv), __fmul_rn(acc[e + 3], inv)) << 16);
+              }
+              dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        named_bar_sync(1, 256);
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace bs

@@ -1,0 +1,131 @@
+"""Drop-in B200 (sm_100a) counterpart of the reference's patches/fp8_hand_sm89.py.
+
+Same surface, same meaning, so the three SGLang hooks installed by
+patches/apply_sglang_fp8_hand_gemm.py (:26-33 GEMM entry, :45-56 MLP forward, :59-65 loader) can
+import this module instead:
+
+  ENABLED / FUSED_ENABLED / FUSED_MIN_M   env switches SGLANG_FP8_HAND_GEMM, SGLANG_FP8_HAND_FUSED,
+                                          SGLANG_FP8_HAND_FUSED_MIN_M (H:41-43)
+  select(N, M) -> dict                    tile choice of an M x N product (H:74-81)
+  precompile() -> list[str]               build step, never on the request path (H:596-611)
+  relayout(model)                         tile-first weight pre-pack after loading (H:652-672)
+  fused_gate_up(proj, x) -> (Q, Qs)|None  fused MLP front half (H:675-701)
+  matmul(A, B, C, As, Bs, M, N, K, block_size) -> bool   GEMM hook (H:704-719)
+
+Differences that follow from the hardware, not from the API:
+  * the capability gate is sm_100 (B200) instead of sm_89;
+  * any K and N that are multiples of 128 are eligible (the reference compiled cubins for
+    K in {5120, 6144, 17408} only, H:46 and H:664);
+  * the fused kernel covers every M, so FUSED_MIN_M defaults to 1 (the reference defaults to
+    1024 because its fused kernel lost to the 3-kernel chain below M=1024 on the 4090);
+  * the activation quant that feeds the fused kernel is this library's CUDA kernel instead of
+    SGLang's Triton per_token_group_quant_fp8 (H:690-693).
+"""
+from __future__ import annotations
+
+import logging
+import os
+
+import torch
+from torch.nn import Parameter
+
+from . import _build, _native, ops
+
+logger = logging.getLogger(__name__)
+
+ENABLED = os.getenv("SGLANG_FP8_HAND_GEMM", "0") == "1"
+FUSED_ENABLED = ENABLED and os.getenv("SGLANG_FP8_HAND_FUSED", "1") == "1"
+FUSED_MIN_M = int(os.getenv("SGLANG_FP8_HAND_FUSED_MIN_M", "1"))
+
+BK = 128
+CAPABILITY = (10, 0)
+DECODE_MAX_M = 128           # M <= 128 runs the swap-AB split-K kernel
+PREFILL = dict(kind="prefill", BM=128, BN=256, BK=BK, stages=4, group_m=16, threads=384)
+
+
+def select(N: int, M: int) -> dict:
+    """Tile of an M x N product: the prefill tcgen05 tile for M > 128, else the decode
+    (swap-AB, weights as the MMA's M=128 side, tokens padded to a multiple of 16)."""
+    if M > DECODE_MAX_M:
+        return dict(PREFILL)
+    ntp = max(16, (M + 15) // 16 * 16)
+    return dict(kind="decode", BM=BK, NTP=ntp, BK=BK, split="stream-k", threads=256)
+
+
+def precompile() -> list[str]:
+    """Builds the sm_100a library (only when a source is newer than the build)."""
+    return [str(_build.build())]
+
+
+def _is_b200() -> bool:
+    return torch.cuda.is_available() and torch.cuda.get_device_capability(0) == CAPABILITY
+
+
+def eligible(name: str, weight: torch.Tensor, scale: torch.Tensor | None) -> bool:
+    """Weights this path takes over at relayout time: e4m3 [N, K] with a [N/128, K/128] fp32 block
+    scale, N and K multiples of 128; lm_head stays where it is, as in H:661."""
+    if scale is None or weight is None or weight.dtype != torch.float8_e4m3fn or "lm_head" in name:
+        return False
+    if weight.dim() != 2:
+        return False
+    N, K = weight.shape
+    return N % BK == 0 and K % BK == 0 and tuple(scale.shape) == (N // BK, K // BK)
+
+
+def relayout(model: torch.nn.Module) -> None:
+    """Moves every eligible FP8 linear to tile-first storage. The parameter keeps its shape on the
+    meta device, so nothing can read the old layout by accident (H:652-672)."""
+    if not ENABLED or not _is_b200():
+        return
+    moved = 0
+    for name, module in model.named_modules():
+        weight = getattr(module, "weight", None)
+        scale = getattr(module, "weight_scale_inv", None)
+        if weight is None or getattr(weight, "tiles", None) is not None:
+            continue
+        if not eligible(name, weight, scale):
+            if isinstance(weight, torch.Tensor) and weight.dtype == torch.float8_e4m3fn:
+                logger.info("FP8 hand: %s %s stays on the row-major path", name, tuple(weight.shape))
+            continue
+        N, K = weight.shape
+        tiles = ops.pack_tiles(weight.data)
+        module.weight = Parameter(torch.empty(N, K, dtype=torch.float8_e4m3fn, device="meta"), requires_grad=False)
+        module.weight.tiles = tiles
+        moved += 1
+    torch.cuda.empty_cache()
+    logger.info("FP8 hand: %d linears tile first", moved)
+
+
+def fused_gate_up(proj, x: torch.Tensor):
+    """Returns (q, scale) for down_proj, or None to run the separate kernels (H:675-701)."""
+    if not FUSED_ENABLED or x.dtype != torch.bfloat16 or x.ndim != 2 or x.shape[0] < FUSED_MIN_M:
+        return None
+    weight = getattr(proj, "weight", None)
+    scale = getattr(proj, "weight_scale_inv", None)
+    tiles = getattr(weight, "tiles", None)
+    if tiles is None or scale is None or scale.ndim != 2:
+        return None
+    N, K = weight.shape
+    if K % BK or N % (2 * BK) or getattr(proj, "bias", None) is not None:
+        return None
+    A, As = ops.group_quant(x, BK)
+    return ops.gemm_silu_quant(A, tiles, As, scale, b_tiled=True)
+
+
+def matmul(A, B, C, As, Bs, M, N, K, block_size) -> bool:
+    """Launches C = A @ B^T and returns True, or returns False for a weight that was not
+    relayouted (H:704-719). C may be bf16 (the reference's only output) or fp32."""
+    tiles = getattr(B, "tiles", None)
+    if tiles is None:
+        return False
+    if block_size is not None and list(block_size) != [BK, BK]:
+        raise ValueError(f"block_size {block_size}: only [128, 128] weight blocks exist on this path")
+    if tiles.shape[0] * BK != N or tiles.shape[1] * BK != K:
+        raise ValueError(f"tiles {tuple(tiles.shape)} do not match N={N}, K={K}")
+    ops.gemm(A, tiles, As, Bs, b_tiled=True, out=C, out_dtype=C.dtype)
+    return True
+
+
+def status(clear: bool = True) -> int:
+    """Device status word (0 = no kernel reported a bounded-wait timeout); synchronises."""
+    return _native.status(clear)

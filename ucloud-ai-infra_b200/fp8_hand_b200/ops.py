@@ -1,0 +1,134 @@
+"""Tensor-level entry points over the C-ABI: activation quant, weight pre-pack, block-scaled FP8
+GEMM and the fused gate_up + SiLU*up + quant front half.
+
+All functions take CUDA tensors, launch on the current stream of the tensors' device, never
+synchronise and never fall back: a tensor outside the contract raises ValueError, a library
+failure raises RuntimeError.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+E4M3 = torch.float8_e4m3fn
+BLOCK = 128
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        _need(t.is_cuda, "tensors must be on a CUDA device (this path has no CPU implementation)")
+        _need(t.device == dev, "all tensors must be on the same device")
+    return dev
+
+
+def _as_bytes(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.uint8 else t.view(torch.uint8)
+
+
+def group_quant(x: torch.Tensor, group_size: int = BLOCK) -> tuple[torch.Tensor, torch.Tensor]:
+    """x bf16 [..., K] -> (A e4m3 [..., K], As fp32 [..., K/128]); per 1x128 group
+    As = max(amax/448, 1e-12), A = e4m3(x / As)."""
+    _need(group_size == BLOCK, "only 128-wide groups are supported")
+    _need(x.dtype == torch.bfloat16, "x must be bf16")
+    dev = _cuda(x)
+    K = x.shape[-1]
+    _need(K % BLOCK == 0, "K must be a multiple of 128")
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    A = torch.empty((M, K), dtype=E4M3, device=dev)
+    As = torch.empty((M, K // BLOCK), dtype=torch.float32, device=dev)
+    with _native.device_guard(dev):
+        _native.check(_native.lib().bs_fp8_group_quant(
+            x2.data_ptr(), x2.stride(0), A.data_ptr(), As.data_ptr(), M, K, _native.stream_handle(dev)),
+            "bs_fp8_group_quant")
+    return A.view(*x.shape[:-1], K), As.view(*x.shape[:-1], K // BLOCK)
+
+
+def pack_tiles(weight: torch.Tensor) -> torch.Tensor:
+    """e4m3 weight [N, K] -> tile-first bytes [N/128, K/128, 128, 128] (H:667 layout)."""
+    _need(weight.dim() == 2 and weight.dtype in (E4M3, torch.uint8), "weight must be e4m3 [N, K]")
+    dev = _cuda(weight)
+    N, K = weight.shape
+    _need(N % BLOCK == 0 and K % BLOCK == 0, "N and K must be multiples of 128")
+    w = _as_bytes(weight.contiguous())
+    tiles = torch.empty((N // BLOCK, K // BLOCK, BLOCK, BLOCK), dtype=torch.uint8, device=dev)
+    with _native.device_guard(dev):
+        _native.check(_native.lib().bs_fp8_pack_tiles(w.data_ptr(), tiles.data_ptr(), N, K,
+                                                      _native.stream_handle(dev)), "bs_fp8_pack_tiles")
+    return tiles
+
+
+def _weight_geometry(B: torch.Tensor, b_tiled: bool) -> tuple[int, int]:
+    if b_tiled:
+        _need(B.dim() == 4 and tuple(B.shape[2:]) == (BLOCK, BLOCK) and B.dtype in (torch.uint8, E4M3),
+              "tile-first weights must be [N/128, K/128, 128, 128] bytes")
+        return B.shape[0] * BLOCK, B.shape[1] * BLOCK
+    _need(B.dim() == 2 and B.dtype in (E4M3, torch.uint8), "row-major weights must be e4m3 [N, K]")
+    return B.shape[0], B.shape[1]
+
+
+def _check_operands(A, B, As, Bs, b_tiled):
+    _need(A.dtype in (E4M3, torch.uint8), "A must be e4m3")
+    dev = _cuda(A, B, As, Bs)
+    N, K = _weight_geometry(B, b_tiled)
+    _need(A.shape[-1] == K, f"A has K={A.shape[-1]}, weights have K={K}")
+    A2 = A.reshape(-1, K)
+    M = A2.shape[0]
+    _need(As.dtype == torch.float32 and Bs.dtype == torch.float32, "scales must be fp32")
+    _need(As.numel() == M * (K // BLOCK), "As must be [M, K/128]")
+    _need(tuple(Bs.shape) == (N // BLOCK, K // BLOCK), "Bs must be [N/128, K/128]")
+    _need(B.is_contiguous(), "weights must be contiguous")
+    if not A2.is_contiguous():
+        A2 = A2.contiguous()
+    return dev, A2, As.reshape(M, K // BLOCK).contiguous(), Bs.contiguous(), M, N, K
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, *, b_tiled: bool = False,
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """C[m, n] = sum_kb (A . B)[m, n, kb] * As[m, kb] * Bs[n/128, kb] -> out [..., N] (bf16 or fp32)."""
+    dev, A2, As2, Bs2, M, N, K = _check_operands(A, B, As, Bs, b_tiled)
+    if out is None:
+        out = torch.empty((*A.shape[:-1], N), dtype=out_dtype, device=dev)
+    _need(out.dtype in (torch.bfloat16, torch.float32), "output must be bf16 or fp32")
+    _need(out.device == dev and out.shape[-1] == N and out.numel() == M * N, "output must be [..., N]")
+    out2 = out.view(M, N)
+    _need(out2.stride(-1) == 1, "output rows must be contiguous")
+    ldc = out2.stride(0) if M > 1 else N
+    lib = _native.lib()
+    with _native.device_guard(dev):
+        ws_bytes = lib.bs_fp8_workspace_bytes(M, N, K, 0)
+        ws = _native.workspace(dev, ws_bytes)
+        _native.check(lib.bs_fp8_gemm(
+            A2.data_ptr(), _as_bytes(B).data_ptr(), out2.data_ptr(), As2.data_ptr(), Bs2.data_ptr(), M, N, K, ldc,
+            int(b_tiled), 0 if out.dtype == torch.bfloat16 else 1, _native.ptr(ws),
+            0 if ws is None else ws.numel(), _native.stream_handle(dev)), "bs_fp8_gemm")
+    return out
+
+
+def gemm_silu_quant(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, *,
+                    b_tiled: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """gate_up GEMM + SiLU(gate)*up + per-token-group quant: B holds [gate; up] (2I rows).
+    Returns Q e4m3 [..., I] and Qs fp32 [..., I/128]."""
+    dev, A2, As2, Bs2, M, N2, K = _check_operands(A, B, As, Bs, b_tiled)
+    _need(N2 % (2 * BLOCK) == 0, "gate_up rows must be a multiple of 256")
+    inter = N2 // 2
+    Q = torch.empty((*A.shape[:-1], inter), dtype=E4M3, device=dev)
+    Qs = torch.empty((*A.shape[:-1], inter // BLOCK), dtype=torch.float32, device=dev)
+    lib = _native.lib()
+    with _native.device_guard(dev):
+        ws_bytes = lib.bs_fp8_workspace_bytes(M, N2, K, 1)
+        ws = _native.workspace(dev, ws_bytes)
+        _native.check(lib.bs_fp8_gemm_silu_quant(
+            A2.data_ptr(), _as_bytes(B).data_ptr(), Q.data_ptr(), As2.data_ptr(), Bs2.data_ptr(), Qs.data_ptr(),
+            M, N2, K, int(b_tiled), _native.ptr(ws), 0 if ws is None else ws.numel(),
+            _native.stream_handle(dev)), "bs_fp8_gemm_silu_quant")
+    return Q, Qs

@@ -1,0 +1,102 @@
+"""Tensor-parallel MLP over NCCL: one process per GPU inside one 8 x B200 box.
+
+The reference runs on one GPU (scripts/run_sglang_48g.sh:117, `--tp-size 1`); this is the
+B200-side extension the north star asks for:
+
+  gate_up  column-parallel, no collective. Rank r keeps gate rows [r*I/tp, (r+1)*I/tp) and the
+           same up rows, packed as [gate_r; up_r], so the fused kernel's "up starts at N2/2"
+           layout (patches/fp8_hand_sm89.py:450) holds per rank. I/tp is a multiple of 128, so
+           no 128x128 scale block straddles two ranks.
+  down     row-parallel over its K = I: rank r keeps columns [r*I/tp, (r+1)*I/tp) of W_down
+           and the matching scale columns. The fused kernel's quant groups (128 wide) line up
+           with those columns, so each rank's (Q_r, Qs_r) is exactly its slice of the 1-GPU
+           (Q, Qs).
+  reduce   one all_reduce(sum) of the [M, H] partials per MLP, fp32 by default (bf16 optional),
+           on the compute stream.
+
+The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
+the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
+sharding and the collective without a GPU.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+BLOCK = 128
+
+
+@dataclass
+class MLPShard:
+    gate_up: torch.Tensor        # e4m3 [2 * I/tp, H] (or tile-first bytes)
+    gate_up_scale: torch.Tensor  # fp32 [2 * I/tp / 128, H / 128]
+    down: torch.Tensor           # e4m3 [H, I/tp]   (or tile-first bytes)
+    down_scale: torch.Tensor     # fp32 [H / 128, I/tp / 128]
+    tiled: bool = False
+
+
+def shard_gate_up(w: torch.Tensor, s: torch.Tensor, rank: int, world: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """[gate; up] rows of the full gate_up weight -> this rank's [gate_r; up_r]."""
+    n2, _ = w.shape
+    inter = n2 // 2
+    if inter % (BLOCK * world):
+        raise ValueError(f"intermediate size {inter} is not a multiple of 128 * tp={world}")
+    per = inter // world
+    u8 = w.view(torch.uint8)
+    rows = torch.cat([u8[rank * per:(rank + 1) * per], u8[inter + rank * per:inter + (rank + 1) * per]])
+    pb = per // BLOCK
+    ib = inter // BLOCK
+    srows = torch.cat([s[rank * pb:(rank + 1) * pb], s[ib + rank * pb:ib + (rank + 1) * pb]])
+    return rows.view(torch.float8_e4m3fn).contiguous(), srows.contiguous()
+
+
+def shard_down(w: torch.Tensor, s: torch.Tensor, rank: int, world: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Columns [r*I/tp, (r+1)*I/tp) of W_down [H, I] and of its scales."""
+    _, inter = w.shape
+    if inter % (BLOCK * world):
+        raise ValueError(f"intermediate size {inter} is not a multiple of 128 * tp={world}")
+    per = inter // world
+    pb = per // BLOCK
+    cols = w.view(torch.uint8)[:, rank * per:(rank + 1) * per].contiguous().view(torch.float8_e4m3fn)
+    return cols, s[:, rank * pb:(rank + 1) * pb].contiguous()
+
+
+def make_shard(gate_up, gate_up_scale, down, down_scale, rank: int, world: int, device=None,
+               tiled: bool = True, compute=None) -> MLPShard:
+    gw, gs = shard_gate_up(gate_up, gate_up_scale, rank, world)
+    dw, ds = shard_down(down, down_scale, rank, world)
+    if device is not None:
+        gw, gs, dw, ds = (t.to(device) for t in (gw, gs, dw, ds))
+    if tiled:
+        if compute is None:
+            from . import ops as compute
+        gw, dw = compute.pack_tiles(gw), compute.pack_tiles(dw)
+    return MLPShard(gw, gs, dw, ds, tiled)
+
+
+class TensorParallelMLP:
+    """x [M, H] bf16 (replicated) -> quant -> fused gate_up_r -> down_r -> all_reduce -> [M, H]."""
+
+    def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.float32, compute=None):
+        if compute is None:
+            from . import ops as compute
+        self.shard = shard
+        self.group = group
+        self.partial_dtype = partial_dtype
+        self.compute = compute
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def partial(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's [M, H] contribution (before the reduction)."""
+        c, s = self.compute, self.shard
+        A, As = c.group_quant(x)
+        Q, Qs = c.gemm_silu_quant(A, s.gate_up, As, s.gate_up_scale, b_tiled=s.tiled)
+        return c.gemm(Q, s.down, Qs, s.down_scale, b_tiled=s.tiled, out_dtype=self.partial_dtype)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        part = self.partial(x)
+        if self.world > 1:
+            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        return part.to(torch.bfloat16)
