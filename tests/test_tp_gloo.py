@@ -1,0 +1,118 @@
+"""CPU, world_size 2 over gloo: the tensor-parallel MLP's sharding and its all_reduce.
+
+The per-rank math is injected as the oracle (tests only) so the host logic of fp8_hand_b200.tp
+(column-parallel gate_up, row-parallel down_proj, sum of partials) runs on CPU ranks and is
+compared with the unsharded oracle MLP.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+H, INTER, M = 256, 512, 8
+
+
+class OracleCompute:
+    """Per-rank compute with the ops interface, backed by the CPU oracle (row-major weights)."""
+
+    @staticmethod
+    def group_quant(x):
+        return O.group_quant(x)
+
+    @staticmethod
+    def gemm_silu_quant(A, B, As, Bs, b_tiled=False):
+        assert not b_tiled
+        q, s, _ = O.fused_gate_up(A, B, As, Bs)
+        return q, s
+
+    @staticmethod
+    def gemm(A, B, As, Bs, b_tiled=False, out_dtype=torch.float32):
+        assert not b_tiled
+        return O.blockwise_matmul(A, B, As, Bs).to(out_dtype)
+
+    @staticmethod
+    def pack_tiles(w):
+        return O.relayout_tiles(w)
+
+
+def _inputs():
+    gu, gus = O.make_weight(2 * INTER, H, seed=1)
+    dn, dns = O.make_weight(H, INTER, seed=2)
+    x = O.make_activation(M, H, seed=3)
+    return gu, gus, dn, dns, x
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from fp8_hand_b200 import tp
+        gu, gus, dn, dns, x = _inputs()
+        shard = tp.make_shard(gu, gus, dn, dns, rank, world, tiled=False, compute=OracleCompute)
+        mlp = tp.TensorParallelMLP(shard, compute=OracleCompute)
+        out = mlp(x)
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shards_reassemble_the_weights():
+    from fp8_hand_b200 import tp
+    gu, gus, dn, dns, _ = _inputs()
+    for world in (2, 4):
+        parts = [tp.shard_gate_up(gu, gus, r, world) for r in range(world)]
+        gate = torch.cat([p[0].view(torch.uint8)[: INTER // world] for p in parts])
+        up = torch.cat([p[0].view(torch.uint8)[INTER // world:] for p in parts])
+        assert torch.equal(torch.cat([gate, up]), gu.view(torch.uint8))
+        assert torch.equal(torch.cat([p[1][: INTER // world // 128] for p in parts]), gus[: INTER // 128])
+        cols = [tp.shard_down(dn, dns, r, world) for r in range(world)]
+        assert torch.equal(torch.cat([c[0].view(torch.uint8) for c in cols], dim=1), dn.view(torch.uint8))
+        assert torch.equal(torch.cat([c[1] for c in cols], dim=1), dns)
+    with pytest.raises(ValueError):
+        tp.shard_gate_up(gu, gus, 0, 3)
+
+
+def test_rank_quant_groups_are_slices_of_the_full_output():
+    """Each rank's fused output (Q_r, Qs_r) equals its column slice of the 1-GPU output."""
+    from fp8_hand_b200 import tp
+    gu, gus, _, _, x = _inputs()
+    A, As = O.group_quant(x)
+    q_full, s_full, _ = O.fused_gate_up(A, gu, As, gus)
+    world = 2
+    for r in range(world):
+        w, s = tp.shard_gate_up(gu, gus, r, world)
+        q, qs, _ = O.fused_gate_up(A, w, As, s)
+        per = INTER // world
+        assert torch.equal(q.view(torch.uint8), q_full.view(torch.uint8)[:, r * per:(r + 1) * per])
+        assert torch.equal(qs, s_full[:, r * per // 128:(r + 1) * per // 128])
+
+
+def test_tp2_gloo_matches_single_rank():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    outs = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    gu, gus, dn, dns, x = _inputs()
+    A, As = O.group_quant(x)
+    Q, Qs, _ = O.fused_gate_up(A, gu, As, gus)
+    ref = O.blockwise_matmul(Q, dn, Qs, dns)
+    assert torch.equal(outs[0], outs[1])
+    assert O.max_rel_error(outs[0].float(), ref) <= 1e-2

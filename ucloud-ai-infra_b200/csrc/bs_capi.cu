@@ -355,4 +355,16 @@ int bs_fp8_abi_version(void) { return 1; }
 
 const char* bs_fp8_last_cuda_error(void) { return g_last_cuda_error; }
 
+#ifdef BS_TRACE
+// Profiling builds only (-DBS_TRACE): copies and clears the stage counters of the current device.
+int bs_fp8_trace_read(unsigned long long* out, int n) {
+  if (!out || n <= 0 || n > 64) return BS_ERR_ARG;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BS_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(out, bs::g_bs_trace, sizeof(unsigned long long) * n) != cudaSuccess) return BS_ERR_CUDA;
+  unsigned long long zero[64] = {0};
+  if (cudaMemcpyToSymbol(bs::g_bs_trace, zero, sizeof(zero)) != cudaSuccess) return BS_ERR_CUDA;
+  return BS_OK;
+}
+#endif
+
 }  // extern "C"

@@ -90,6 +90,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Same contract as mbar_wait, but polls with the non-suspending test_wait: for the MMA <-> promotion
+// handoffs, where a suspended waiter's wake-up latency sits on the critical path of every K block.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                               int code, uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_test_wait(bar, parity)) return true;
+  if (*abort) return false;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((++spins & 1023u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        atomicCAS(status, 0, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA (per-CTA, never multicast)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -176,6 +209,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]),
+        "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+        "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]),
+        "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]),
+        "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -230,12 +282,68 @@ __device__ __forceinline__ void regs_decrease() {
 // Keeps the compiler from hoisting loads across this point (bounds live registers).
 __device__ __forceinline__ void compiler_fence() { asm volatile("" ::: "memory"); }
 
+// ---------------------------------------------------------------- stage counters
+// Built only with -DBS_TRACE (a profiling build; the product build compiles these to nothing).
+// Each role accumulates clock64() cycles per pipeline segment in registers and adds them to
+// g_bs_trace once at the end, so the counters cost nothing inside the loops but two clock reads.
+#ifdef BS_TRACE
+__device__ unsigned long long g_bs_trace[64];
+#define BS_TR_DECL(n)        \
+  long long bs_tr[n] = {0};  \
+  const long long bs_tr_t0 = clock64(); \
+  long long bs_tr_mark = bs_tr_t0
+#define BS_TR_MARK() (bs_tr_mark = clock64())
+#define BS_TR_ADD(i)                   \
+  do {                                 \
+    const long long bs_tr_now = clock64(); \
+    bs_tr[i] += bs_tr_now - bs_tr_mark;    \
+    bs_tr_mark = bs_tr_now;                \
+  } while (0)
+#define BS_TR_FLUSH(base, n)                                                                    \
+  do {                                                                                          \
+    for (int bs_tr_i = 0; bs_tr_i < (n); ++bs_tr_i)                                             \
+      atomicAdd(&g_bs_trace[(base) + bs_tr_i], static_cast<unsigned long long>(bs_tr[bs_tr_i])); \
+    atomicAdd(&g_bs_trace[(base) + (n)], static_cast<unsigned long long>(clock64() - bs_tr_t0)); \
+    atomicAdd(&g_bs_trace[(base) + (n) + 1], 1ull);                                             \
+  } while (0)
+#else
+#define BS_TR_DECL(n) \
+  do {                \
+  } while (0)
+#define BS_TR_MARK() \
+  do {               \
+  } while (0)
+#define BS_TR_ADD(i) \
+  do {               \
+  } while (0)
+#define BS_TR_FLUSH(base, n) \
+  do {                       \
+  } while (0)
+#endif
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 __device__ __forceinline__ float ldg_f32(const float* p) { return __ldg(p); }
+
+// ---------------------------------------------------------------- packed fp32 pairs
+// Accumulators are kept as pairs in 64-bit registers so the promotion runs on the packed
+// fma.rn.f32x2 (sm_100): each lane is an ordinary fma.rn.f32, so results are bit-identical to
+// two scalar fmaf calls while the instruction count halves.
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+
+// acc.{lo,hi} = fma({p0, p1}, s.{lo,hi}, acc.{lo,hi}), round to nearest even per lane.
+__device__ __forceinline__ void ffma2(uint64_t& acc, uint32_t p0, uint32_t p1, uint64_t s) {
+  asm("{\n\t.reg .b64 p;\n\tmov.b64 p, {%1, %2};\n\tfma.rn.f32x2 %0, p, %3, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(p0), "r"(p1), "l"(s));
+}
 
 // Two floats -> two e4m3 bytes (round to nearest even, saturate to +-448), low byte = a.
 __device__ __forceinline__ uint32_t f2_to_e4m3x2(float a, float b) {

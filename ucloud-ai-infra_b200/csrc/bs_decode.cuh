@@ -63,6 +63,21 @@ struct DecodeCfg {
   static_assert(kTmemCols <= 512, "TMEM budget");
 };
 
+// Loads N consecutive TMEM columns (N a multiple of 16, at most 64) of this warp's 32 lanes into
+// v[0..N) with every load in flight at once, then waits once.
+template <int N>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&v)[64]) {
+  static_assert(N % 16 == 0 && N <= 64, "column group");
+  if constexpr (N == 64) {
+    tmem_ld64(taddr, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c + 32 <= N; c += 32) tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&v[c]));
+    if constexpr (N % 32 == 16) tmem_ld16(taddr + (N - 16), *reinterpret_cast<uint32_t(*)[16]>(&v[N - 16]));
+  }
+  tmem_ld_wait();
+}
+
 // CTA that owns unit u when U units are split into G contiguous ranges [c*U/G, (c+1)*U/G).
 __device__ __forceinline__ int unit_owner(long long u, long long U, int G) {
   return static_cast<int>(((u + 1) * G - 1) / U);
@@ -214,72 +229,81 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
     const int r = q * 32 + lane;      // weight row inside the 128-row block
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
 
-    // Scale product of unit u for token i: As[i, kb] * Bs[nb, kb] (0 for padding tokens).
-    auto scale_of = [&](long long u, int i) -> float {
-      const int t = static_cast<int>(u / KB);
-      const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
-      const int nb = wg == 0 ? t : t + I_blk;
-      if (i >= M) return 0.f;
-      return __fmul_rn(ldg_f32(p.As + static_cast<size_t>(i) * KB + kb), ldg_f32(p.Bs + static_cast<size_t>(nb) * KB + kb));
+    // Scale operands of unit u for token i: As[i, kb] and Bs[nb, kb]. The loads are issued from
+    // always-valid addresses (last unit of the range, token 0 for padding tokens) and without a
+    // select, because any instruction that consumed the result right away would wait for it.
+    // The product and the padding mask are applied when the pair is stored to the shared ring,
+    // two units later.
+    const int ri = r < M ? r : 0;
+    const bool r_live = r < M;
+    struct ScalePair {
+      float a, b;
     };
+    auto load_scales = [&](long long u) -> ScalePair {
+      const long long uc = u < u1 ? u : u1 - 1;
+      const int t = static_cast<int>(uc / KB);
+      const int kb = static_cast<int>(uc - static_cast<long long>(t) * KB);
+      const int nb = wg == 0 ? t : t + I_blk;
+      return {ldg_f32(p.As + static_cast<size_t>(ri) * KB + kb), ldg_f32(p.Bs + static_cast<size_t>(nb) * KB + kb)};
+    };
+    auto scale_value = [&](const ScalePair& s) -> float { return r_live ? __fmul_rn(s.a, s.b) : 0.f; };
 
-    if (r < NTP) ring[(0 * NWG + wg) * NTP + r] = (u0 < u1) ? scale_of(u0, r) : 0.f;
-    float nxt = (r < NTP && u0 + 1 < u1) ? scale_of(u0 + 1, r) : 0.f;
+    // Unit u's body stores the scale for u+1 (loaded two units earlier) into the ring and loads
+    // the operands for u+3 into the registers it just freed. Two fixed register pairs alternate.
+    if (r < NTP) ring[(0 * NWG + wg) * NTP + r] = (u0 < u1) ? scale_value(load_scales(u0)) : 0.f;
+    ScalePair nxt_a = load_scales(u0 + 1);
+    ScalePair nxt_b = load_scales(u0 + 2);
     named_bar_sync(1, NPROMO);
 
-    float acc[NTP];
+    uint64_t acc[NTP / 2];  // token pairs (2i, 2i+1)
 #pragma unroll
-    for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
+    for (int i = 0; i < NTP / 2; ++i) acc[i] = 0;
 
     int b = 0;
     uint32_t pph = 0;
     bool ok = true;
     int slot = 0;                                   // ring slot of the current unit
     int seg_kb0 = static_cast<int>(u0 % KB);
-    for (long long u = u0; u < u1; ++u) {
+    constexpr int G0 = NTP < 64 ? NTP : 64;         // first column group
+    constexpr int G1 = NTP - G0;                    // second column group (NTP > 64)
+    auto unit_body = [&](long long u, ScalePair& nxt) {
       const int t = static_cast<int>(u / KB);
       const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
       const int slot_next = slot == 2 ? 0 : slot + 1;
-      if (r < NTP) ring[(slot_next * NWG + wg) * NTP + r] = nxt;
-      nxt = (r < NTP && u + 2 < u1) ? scale_of(u + 2, r) : 0.f;
+      if (r < NTP) ring[(slot_next * NWG + wg) * NTP + r] = scale_value(nxt);
+      nxt = load_scales(u + 3);
       named_bar_sync(1, NPROMO);
 
       if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
       if (ok) {
         tc_fence_after();
         const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * NWG * NTP + wg * NTP);
-        const float4* sc4 = reinterpret_cast<const float4*>(ring + (slot * NWG + wg) * NTP);
+        const ulonglong2* sc = reinterpret_cast<const ulonglong2*>(ring + (slot * NWG + wg) * NTP);
+        uint32_t v[64];
+        tmem_load_cols<G0>(tbase, v);
+        if constexpr (G1 == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[b]);
+        }
 #pragma unroll
-        for (int c0 = 0; c0 + 32 <= NTP; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c0, v);
-          tmem_ld_wait();
+        for (int i = 0; i < G0; i += 4) {
+          const ulonglong2 s2 = sc[i / 4];
+          ffma2(acc[i / 2], v[i], v[i + 1], s2.x);
+          ffma2(acc[i / 2 + 1], v[i + 2], v[i + 3], s2.y);
+        }
+        if constexpr (G1 > 0) {
+          tmem_load_cols<G1>(tbase + G0, v);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[b]);
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 s4 = sc4[(c0 + i) / 4];
-            acc[c0 + i + 0] = fmaf(__uint_as_float(v[i + 0]), s4.x, acc[c0 + i + 0]);
-            acc[c0 + i + 1] = fmaf(__uint_as_float(v[i + 1]), s4.y, acc[c0 + i + 1]);
-            acc[c0 + i + 2] = fmaf(__uint_as_float(v[i + 2]), s4.z, acc[c0 + i + 2]);
-            acc[c0 + i + 3] = fmaf(__uint_as_float(v[i + 3]), s4.w, acc[c0 + i + 3]);
+          for (int i = 0; i < G1; i += 4) {
+            const ulonglong2 s2 = sc[(G0 + i) / 4];
+            ffma2(acc[(G0 + i) / 2], v[i], v[i + 1], s2.x);
+            ffma2(acc[(G0 + i) / 2 + 1], v[i + 2], v[i + 3], s2.y);
           }
         }
-        if constexpr (NTP % 32 == 16) {
-          constexpr int c0 = NTP - 16;
-          uint32_t v[16];
-          tmem_ld16(tbase + c0, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 s4 = sc4[(c0 + i) / 4];
-            acc[c0 + i + 0] = fmaf(__uint_as_float(v[i + 0]), s4.x, acc[c0 + i + 0]);
-            acc[c0 + i + 1] = fmaf(__uint_as_float(v[i + 1]), s4.y, acc[c0 + i + 1]);
-            acc[c0 + i + 2] = fmaf(__uint_as_float(v[i + 2]), s4.z, acc[c0 + i + 2]);
-            acc[c0 + i + 3] = fmaf(__uint_as_float(v[i + 3]), s4.w, acc[c0 + i + 3]);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[b]);
       }
       if (++b == 2) {
         b = 0;
@@ -299,7 +323,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           if (ok) {
 #pragma unroll
             for (int tt = 0; tt < NTP; ++tt)
-              if (tt < M) part[tt * 128] = acc[tt];
+              if (tt < M) part[tt * 128] = (tt & 1) ? hi_f(acc[tt / 2]) : lo_f(acc[tt / 2]);
           }
           __threadfence();
           named_bar_sync(1, NPROMO);
@@ -314,14 +338,16 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           if (finisher) {
             __threadfence();
 #pragma unroll
-            for (int tt = 0; tt < NTP; ++tt) acc[tt] = 0.f;
+            for (int i = 0; i < NTP / 2; ++i) acc[i] = 0;
             for (int cc = c_first; cc <= c_last; ++cc) {
               const int sl = (cc == c_first && (static_cast<long long>(cc) * U / G) < tu0) ? 1 : 0;
               const float* src = p.ws + (static_cast<size_t>(cc * 2 + sl) * NWG + wg) * (NTP * 128) + r;
 #pragma unroll
-              for (int tt = 0; tt < NTP; ++tt) {
-                if (tt < M) acc[tt] += __ldcg(src + tt * 128);
-                if ((tt & 15) == 15) compiler_fence();  // at most 16 loads in flight per thread
+              for (int tt = 0; tt < NTP; tt += 2) {
+                const float x0 = tt < M ? __ldcg(src + tt * 128) : 0.f;
+                const float x1 = tt + 1 < M ? __ldcg(src + (tt + 1) * 128) : 0.f;
+                acc[tt / 2] = pack_f2(lo_f(acc[tt / 2]) + x0, hi_f(acc[tt / 2]) + x1);
+                if ((tt & 15) == 14) compiler_fence();  // at most 16 loads in flight per thread
               }
             }
           }
@@ -334,14 +360,14 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
                 float* C = static_cast<float*>(p.out) + col;
 #pragma unroll
                 for (int tt = 0; tt < NTP; ++tt) {
-                  if (tt < M) *C = acc[tt];
+                  if (tt < M) *C = (tt & 1) ? hi_f(acc[tt / 2]) : lo_f(acc[tt / 2]);
                   C += p.ldc;
                 }
               } else {
                 __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.out) + col;
 #pragma unroll
                 for (int tt = 0; tt < NTP; ++tt) {
-                  if (tt < M) *C = __float2bfloat16_rn(acc[tt]);
+                  if (tt < M) *C = __float2bfloat16_rn((tt & 1) ? hi_f(acc[tt / 2]) : lo_f(acc[tt / 2]));
                   C += p.ldc;
                 }
               }
@@ -351,12 +377,13 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
             // threads per token quantises its 128-wide group.
             if (wg == 1) {
 #pragma unroll
-              for (int tt = 0; tt < NTP; ++tt) xch[tt * 128 + r] = acc[tt];
+              for (int tt = 0; tt < NTP; ++tt) xch[tt * 128 + r] = (tt & 1) ? hi_f(acc[tt / 2]) : lo_f(acc[tt / 2]);
             }
             named_bar_sync(1, NPROMO);
             if (wg == 0) {
 #pragma unroll
-              for (int tt = 0; tt < NTP; ++tt) xch[tt * 128 + r] = silu_mul(acc[tt], xch[tt * 128 + r]);
+              for (int tt = 0; tt < NTP; ++tt)
+                xch[tt * 128 + r] = silu_mul((tt & 1) ? hi_f(acc[tt / 2]) : lo_f(acc[tt / 2]), xch[tt * 128 + r]);
             }
             named_bar_sync(1, NPROMO);
             const int tok = tid >> 1;
@@ -399,9 +426,13 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           }
         }
 #pragma unroll
-        for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
+        for (int i = 0; i < NTP / 2; ++i) acc[i] = 0;
         seg_kb0 = 0;
       }
+    };
+    for (long long u = u0; u < u1; u += 2) {
+      unit_body(u, nxt_a);
+      if (u + 1 < u1) unit_body(u + 1, nxt_b);
     }
   }
 

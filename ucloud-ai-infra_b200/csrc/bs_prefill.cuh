@@ -143,16 +143,19 @@ __global__ void __launch_bounds__(384, 1)
       int s = 0;
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
+      BS_TR_DECL(1);
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int tm, tn;
         prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
         const int nb0 = FUSED ? tn : 2 * tn;
         const int nb1 = FUSED ? tn + I_blk : 2 * tn + 1;
         for (int kb = 0; kb < KB; ++kb) {
+          BS_TR_MARK();
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
+          BS_TR_ADD(0);
           uint8_t* st = smem + s * Cfg::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
           tma_load_2d(st, &tmA, &full[s], kb * 128, tm * 128, pol_a);
@@ -166,6 +169,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       }
+      BS_TR_FLUSH(0, 1);
       if (!ok) {
         // Leave no copy in flight: wait (bounded) for the last fill of every stage.
         for (int i = 0; i < S; ++i)
@@ -180,13 +184,20 @@ __global__ void __launch_bounds__(384, 1)
       int s = 0, b = 0;
       uint32_t ph = 0, pph = 0;
       bool ok = true;
+      BS_TR_DECL(2);
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull) ||
-              !mbar_wait(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) {
+          BS_TR_MARK();
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) {
             ok = false;
             break;
           }
+          BS_TR_ADD(0);
+          if (!mbar_wait_spin(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) {
+            ok = false;
+            break;
+          }
+          BS_TR_ADD(1);
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t b0 = a0 + Cfg::kABytes;
@@ -206,6 +217,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       }
+      BS_TR_FLUSH(4, 2);
       // Every MMA issued so far completes before TMEM is released.
       mma_commit(drain);
       mbar_wait(drain, 0, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
@@ -223,6 +235,7 @@ __global__ void __launch_bounds__(384, 1)
     int b = 0;
     uint32_t pph = 0;
     bool ok = true;
+    BS_TR_DECL(4);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int tm, tn;
       prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
@@ -233,46 +246,65 @@ __global__ void __launch_bounds__(384, 1)
       const float* as_row = p.As + static_cast<size_t>(row_ok ? row : 0) * KB;
       const float* bs_row = p.Bs + static_cast<size_t>(col_ok ? nb : 0) * KB;
 
-      float acc[128];
+      uint64_t acc[64];  // column pairs (2i, 2i+1) of this thread's 128 columns
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      for (int i = 0; i < 64; ++i) acc[i] = 0;
 
-      // Scale prefetch two K blocks ahead (L2 latency is about one K block of MMA time).
-      float a_n0 = row_ok ? ldg_f32(as_row) : 0.f, b_n0 = col_ok ? ldg_f32(bs_row) : 0.f;
-      float a_n1 = (row_ok && KB > 1) ? ldg_f32(as_row + 1) : 0.f;
-      float b_n1 = (col_ok && KB > 1) ? ldg_f32(bs_row + 1) : 0.f;
+      // Scales come from a 4-slot register ring filled four K blocks ahead. The loop is unrolled
+      // by 4 so each slot is a fixed register: a loaded value is read once, four blocks after its
+      // load was issued, and never copied or selected on (either would wait for the load to
+      // land). Rows past M and the missing half of an odd last column tile read row 0 / block 0:
+      // their A rows and weight rows are zero-filled by TMA, so the partial they scale is zero.
+      float ra[4], rb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ra[j] = ldg_f32(as_row + (j < KB ? j : 0));
+        rb[j] = ldg_f32(bs_row + (j < KB ? j : 0));
+      }
 
-      for (int kb = 0; kb < KB; ++kb) {
-        const float sa = a_n0, sb = b_n0;
-        a_n0 = a_n1;
-        b_n0 = b_n1;
-        if (kb + 2 < KB) {
-          a_n1 = row_ok ? ldg_f32(as_row + kb + 2) : 0.f;
-          b_n1 = col_ok ? ldg_f32(bs_row + kb + 2) : 0.f;
-        }
-        const float sc = __fmul_rn(sa, sb);
-        if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
-        if (ok) {
-          tc_fence_after();
-          const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * 256 + wg * 128);
+      for (int kb0 = 0; kb0 < KB; kb0 += 4) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tbase + c * 32, v);
-            tmem_ld_wait();
+        for (int j = 0; j < 4; ++j) {
+          const int kb = kb0 + j;
+          if (kb < KB) {
+            BS_TR_MARK();
+            const float sc = __fmul_rn(ra[j], rb[j]);
+            if (kb + 4 < KB) {
+              ra[j] = ldg_f32(as_row + kb + 4);
+              rb[j] = ldg_f32(bs_row + kb + 4);
+            }
+            const uint64_t sc2 = pack_f2(sc, sc);
+            BS_TR_ADD(0);
+            if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
+            BS_TR_ADD(1);
+            if (ok) {
+              tc_fence_after();
+              const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * 256 + wg * 128);
+              uint32_t v[64];
+              tmem_ld64(tbase, v);
+              tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(v[i]), sc, acc[c * 32 + i]);
+              for (int i = 0; i < 32; ++i) ffma2(acc[i], v[2 * i], v[2 * i + 1], sc2);
+              tmem_ld64(tbase + 64, v);
+              tmem_ld_wait();
+              // Everything this warp needs from the partial buffer is in registers: hand it back
+              // to the MMA issuer before the second half of the FMAs.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&pempty[b]);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
+              BS_TR_ADD(2);
+            }
+            if (++b == 2) {
+              b = 0;
+              pph ^= 1;
+            }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pempty[b]);
-        }
-        if (++b == 2) {
-          b = 0;
-          pph ^= 1;
         }
       }
 
+      BS_TR_MARK();
       if constexpr (!FUSED) {
         if (ok && row_ok && col_ok) {
           if (p.out_f32) {
@@ -280,15 +312,16 @@ __global__ void __launch_bounds__(384, 1)
                                                     static_cast<size_t>(nb) * 128);
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+              dst[j] = make_float4(lo_f(acc[2 * j]), hi_f(acc[2 * j]), lo_f(acc[2 * j + 1]), hi_f(acc[2 * j + 1]));
           } else {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
                                                   static_cast<size_t>(row) * p.ldc + static_cast<size_t>(nb) * 128);
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              dst[j] = make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
-                                  pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]),
-                                  pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+              dst[j] = make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
           }
         }
       } else {
@@ -298,7 +331,8 @@ __global__ void __launch_bounds__(384, 1)
         if (wg == 1) {
 #pragma unroll
           for (int c4 = 0; c4 < 32; ++c4)
-            x4[r * 32 + (c4 ^ (r & 7))] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+            x4[r * 32 + (c4 ^ (r & 7))] =
+                make_float4(lo_f(acc[2 * c4]), hi_f(acc[2 * c4]), lo_f(acc[2 * c4 + 1]), hi_f(acc[2 * c4 + 1]));
         }
         named_bar_sync(1, 256);
         if (wg == 0) {
@@ -306,12 +340,13 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int c4 = 0; c4 < 32; ++c4) {
             const float4 u = x4[r * 32 + (c4 ^ (r & 7))];
-            acc[4 * c4 + 0] = silu_mul(acc[4 * c4 + 0], u.x);
-            acc[4 * c4 + 1] = silu_mul(acc[4 * c4 + 1], u.y);
-            acc[4 * c4 + 2] = silu_mul(acc[4 * c4 + 2], u.z);
-            acc[4 * c4 + 3] = silu_mul(acc[4 * c4 + 3], u.w);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(acc[4 * c4]), fabsf(acc[4 * c4 + 1])),
-                                     fmaxf(fabsf(acc[4 * c4 + 2]), fabsf(acc[4 * c4 + 3]))));
+            const float y0 = silu_mul(lo_f(acc[2 * c4]), u.x);
+            const float y1 = silu_mul(hi_f(acc[2 * c4]), u.y);
+            const float y2 = silu_mul(lo_f(acc[2 * c4 + 1]), u.z);
+            const float y3 = silu_mul(hi_f(acc[2 * c4 + 1]), u.w);
+            acc[2 * c4] = pack_f2(y0, y1);
+            acc[2 * c4 + 1] = pack_f2(y2, y3);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
           }
           const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
           const float inv = __fdiv_rn(1.0f, scale);
@@ -325,9 +360,9 @@ __global__ void __launch_bounds__(384, 1)
               uint32_t w[4];
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
-                const int e = 16 * j + 4 * h;
-                w[h] = f2_to_e4m3x2(__fmul_rn(acc[e], inv), __fmul_rn(acc[e + 1], inv)) |
-                       (f2_to_e4m3x2(__fmul_rn(acc[e + 2], inv), __fmul_rn(acc[e + 3], inv)) << 16);
+                const int e = 8 * j + 2 * h;  // pair index: columns 16j + 4h .. +3
+                w[h] = f2_to_e4m3x2(__fmul_rn(lo_f(acc[e]), inv), __fmul_rn(hi_f(acc[e]), inv)) |
+                       (f2_to_e4m3x2(__fmul_rn(lo_f(acc[e + 1]), inv), __fmul_rn(hi_f(acc[e + 1]), inv)) << 16);
               }
               dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
             }
@@ -335,7 +370,9 @@ __global__ void __launch_bounds__(384, 1)
         }
         named_bar_sync(1, 256);
       }
+      BS_TR_ADD(3);
     }
+    if (lane == 0 && (warp & 3) == 0) BS_TR_FLUSH(8, 4);
   }
 
   // ------------------------------------------------------------ teardown
