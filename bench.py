@@ -76,7 +76,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
@@ -215,6 +215,10 @@ def run_ours(args, rank, world, device) -> dict | None:
     def step(inp):
         return mlp(inp)
 
+    # Clocks are sampled from the warm-up through the e2e loop (the device-timed region alone is
+    # shorter than nvidia-smi's sampling period).
+    clk = ClockSampler(device.index)
+    clk.__enter__()
     for _ in range(args.warmup):
         step(x)
     torch.cuda.synchronize()
@@ -222,12 +226,11 @@ def run_ours(args, rank, world, device) -> dict | None:
     barrier(world)
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clk:
-        t0.record(stream)
-        for _ in range(args.steps):
-            out = step(x)
-        t1.record(stream)
-        torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(args.steps):
+        out = step(x)
+    t1.record(stream)
+    torch.cuda.synchronize()
     ops.gemm_silu_quant = orig_fused
     barrier(world)
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, device)
@@ -254,6 +257,7 @@ def run_ours(args, rank, world, device) -> dict | None:
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
+    clk.__exit__(None, None, None)
 
     # Decode / verify sizes: fused gate_up (config 2) on this rank's shard, HBM GB/s.
     decode = {}
@@ -356,7 +360,7 @@ class CpuReference:
         return time.perf_counter() - t, mlp_flops(rows)
 
 
-def cpu_baseline_sample(rows: int, reps: int = 2) -> dict:
+def cpu_baseline_sample(rows: int, reps: int = 1) -> dict:
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ref = CpuReference()
@@ -368,7 +372,7 @@ def cpu_baseline_sample(rows: int, reps: int = 2) -> dict:
         flops += f_
     return {"value": round(flops / secs / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{reps} x {rows} of the {M_PREFILL} tokens of the same MLP (weights dequantised per call "
-                      f"as the reference's ref_matmul does, fp32 matmuls), {secs:.1f} s timed"}
+                      f"as the reference's ref_matmul does, fp32 matmuls, all host threads), {secs:.1f} s timed"}
 
 
 def run_reference(args, rank, world) -> dict | None:
@@ -402,7 +406,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--ref-rows", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -115,7 +115,7 @@ size_t decode_ws_bytes(int G, int nwg, int ntp, int tiles) {
 // them exactly the launch register count the split was computed for. The state is keyed on the
 // kernel itself (a template value parameter), since all GEMM kernels share one signature.
 template <auto kernel>
-int prepare_kernel(int smem_bytes, bool split_regs) {
+int prepare_kernel(int smem_bytes, int launch_regs) {
   struct State {
     std::once_flag once[kMaxDevices];
     int rc[kMaxDevices];
@@ -127,12 +127,12 @@ int prepare_kernel(int smem_bytes, bool split_regs) {
     int rc = BS_OK;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) rc = cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
-    if (rc == BS_OK && split_regs) {
+    if (rc == BS_OK && launch_regs > 0) {
       cudaFuncAttributes attr;
       e = cudaFuncGetAttributes(&attr, kernel);
       if (e != cudaSuccess)
         rc = cuda_fail(e, "cudaFuncGetAttributes");
-      else if (attr.numRegs != bs::kLaunchRegs)
+      else if (attr.numRegs != launch_regs)
         rc = BS_ERR_BUILD;
     }
     st.rc[dev] = rc;
@@ -145,7 +145,7 @@ int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const bs::Gemm
                   cudaStream_t s) {
   using Cfg = bs::DecodeCfg<FUSED, NTP>;
   constexpr auto kern = bs::k_decode<FUSED, NTP>;
-  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::kSplitRegs);
+  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::kLaunchRegs);
   if (rc != BS_OK) return rc;
   cudaGetLastError();  // clear an older error so the check below sees this launch only
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmW, tmX, p);
@@ -173,7 +173,7 @@ int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::Gem
                    int num_sms, cudaStream_t s) {
   using Cfg = bs::PrefillCfg<FUSED>;
   constexpr auto kern = bs::k_prefill<FUSED>;
-  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, true);
+  const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::Regs::kLaunch);
   if (rc != BS_OK) return rc;
   const int grid = num_tiles < num_sms ? num_tiles : num_sms;
   cudaGetLastError();

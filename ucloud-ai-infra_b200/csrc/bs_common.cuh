@@ -260,15 +260,22 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
 }
 
 // ---------------------------------------------------------------- register split
-// Warp-specialised kernels launch 384 threads at 168 registers (64,512 of the SM's 65,536).
-// The producer/MMA warpgroup gives registers back and the two promotion warpgroups take them:
-//   128 x 40 + 256 x 232 = 64,512 = 384 x 168.
-// The host refuses to launch such a kernel unless it was built with exactly kLaunchRegs
-// registers, since any other launch count would make the increase wait forever.
-constexpr int kLaunchRegs = 168;
-constexpr int kProducerRegs = 40;
-constexpr int kConsumerRegs = 232;
-static_assert(128 * kProducerRegs + 256 * kConsumerRegs == 384 * kLaunchRegs, "register split must balance");
+// Warp-specialised kernels launch every thread at the same register count; the warpgroup that
+// only issues TMA / MMA instructions then gives registers back (setmaxnreg.dec) and the
+// promotion warpgroups take them (setmaxnreg.inc). An increase draws on the registers the block
+// was launched with, so a split must add up exactly to threads x launch registers, and the host
+// refuses to launch a kernel whose build does not have exactly the launch count it was designed
+// for (any other count would make the increase wait forever).
+template <int kThreads_, int kLaunch_, int kProducer_, int kConsumer_>
+struct RegSplit {
+  static constexpr int kThreads = kThreads_;
+  static constexpr int kLaunch = kLaunch_;
+  static constexpr int kProducer = kProducer_;    // one warpgroup of 128 threads
+  static constexpr int kConsumer = kConsumer_;    // every other thread
+  static_assert(128 * kProducer + (kThreads - 128) * kConsumer == kThreads * kLaunch,
+                "register split must use exactly the registers the block was launched with");
+  static_assert(kLaunch % 8 == 0 && kProducer % 8 == 0 && kConsumer % 8 == 0, "register counts in steps of 8");
+};
 
 template <int N>
 __device__ __forceinline__ void regs_increase() {

@@ -43,6 +43,8 @@ struct DecodeCfg {
   static constexpr int kPromo = 128 * kNwg;
   static constexpr int kThreads = kPromo + 128;
   static constexpr bool kSplitRegs = FUSED;  // 384 threads: registers move to the promotion warps
+  using Regs = RegSplit<384, 168, 40, 232>;   // used when kSplitRegs
+  static constexpr int kLaunchRegs = kSplitRegs ? Regs::kLaunch : 0;
   static constexpr int kWBytes = 16384 * kNwg;
   static constexpr int kXBytes = NTP * 128;
   static constexpr int kStageBytes = ((kWBytes + kXBytes + 1023) / 1024) * 1024;
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
 
   // Each role changes its register budget at the top of its own branch (see k_prefill).
   if (warp >= prod_warp) {
-    if constexpr (Cfg::kSplitRegs) regs_decrease<kProducerRegs>();
+    if constexpr (Cfg::kSplitRegs) regs_decrease<Cfg::Regs::kProducer>();
   if (warp == prod_warp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
     }
   }
   } else {
-    if constexpr (Cfg::kSplitRegs) regs_increase<kConsumerRegs>();
+    if constexpr (Cfg::kSplitRegs) regs_increase<Cfg::Regs::kConsumer>();
     // ------------------------------------------------------------ promotion + epilogue
     // Every promotion thread runs the same sequence of named barriers whether or not the CTA
     // aborted; after an abort only the waits, TMEM reads and stores are skipped.

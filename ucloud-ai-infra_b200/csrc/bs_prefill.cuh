@@ -47,7 +47,8 @@ struct GemmParams {
 
 template <bool FUSED>
 struct PrefillCfg {
-  static constexpr int kThreads = 384;
+  using Regs = RegSplit<384, 168, 40, 232>;
+  static constexpr int kThreads = Regs::kThreads;
   static constexpr int kStages = FUSED ? 3 : 4;
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = 256 * 128;
@@ -80,7 +81,7 @@ __device__ __forceinline__ void load_weight_box(void* dst, const CUtensorMap* ma
 }
 
 template <bool FUSED>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const GemmParams p) {
   using Cfg = PrefillCfg<FUSED>;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(384, 1)
   // Each role changes its register budget at the top of its own branch: code after a merge of
   // the two branches must fit the smaller budget, and only the short teardown follows one.
   if (warp >= 8) {
-    regs_decrease<kProducerRegs>();
+    regs_decrease<Cfg::Regs::kProducer>();
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(384, 1)
             break;
           }
           BS_TR_ADD(0);
-          if (!mbar_wait_spin(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) {
+          if (!mbar_wait(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) {
             ok = false;
             break;
           }
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(384, 1)
     }
   }
   } else {
-    regs_increase<kConsumerRegs>();
+    regs_increase<Cfg::Regs::kConsumer>();
     // ------------------------------------------------------------ promotion + epilogue
     const int wg = warp >> 2;         // 0: columns 0-127 of the tile, 1: columns 128-255
     const int q = warp & 3;           // TMEM lane quarter
@@ -250,57 +251,41 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0;
 
-      // Scales come from a 4-slot register ring filled four K blocks ahead. The loop is unrolled
-      // by 4 so each slot is a fixed register: a loaded value is read once, four blocks after its
-      // load was issued, and never copied or selected on (either would wait for the load to
-      // land). Rows past M and the missing half of an odd last column tile read row 0 / block 0:
-      // their A rows and weight rows are zero-filled by TMA, so the partial they scale is zero.
-      float ra[4], rb[4];
+      // Scales are prefetched two K blocks ahead through a pair of registers. Rows past M and
+      // the missing half of an odd last column tile read row 0 / block 0: their A rows and weight
+      // rows are zero-filled by TMA, so the partial they scale is zero.
+      float a_n0 = ldg_f32(as_row), b_n0 = ldg_f32(bs_row);
+      float a_n1 = ldg_f32(as_row + (KB > 1 ? 1 : 0)), b_n1 = ldg_f32(bs_row + (KB > 1 ? 1 : 0));
+      for (int kb = 0; kb < KB; ++kb) {
+        const float sa = a_n0, sb = b_n0;
+        a_n0 = a_n1;
+        b_n0 = b_n1;
+        if (kb + 2 < KB) {
+          a_n1 = ldg_f32(as_row + kb + 2);
+          b_n1 = ldg_f32(bs_row + kb + 2);
+        }
+        const float sc = __fmul_rn(sa, sb);
+        const uint64_t sc2 = pack_f2(sc, sc);
+        if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * 256 + wg * 128);
+          uint32_t v[64];
+          tmem_ld64(tbase, v);
+          tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ra[j] = ldg_f32(as_row + (j < KB ? j : 0));
-        rb[j] = ldg_f32(bs_row + (j < KB ? j : 0));
-      }
-
-      for (int kb0 = 0; kb0 < KB; kb0 += 4) {
+          for (int i = 0; i < 32; ++i) ffma2(acc[i], v[2 * i], v[2 * i + 1], sc2);
+          tmem_ld64(tbase + 64, v);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[b]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int kb = kb0 + j;
-          if (kb < KB) {
-            BS_TR_MARK();
-            const float sc = __fmul_rn(ra[j], rb[j]);
-            if (kb + 4 < KB) {
-              ra[j] = ldg_f32(as_row + kb + 4);
-              rb[j] = ldg_f32(bs_row + kb + 4);
-            }
-            const uint64_t sc2 = pack_f2(sc, sc);
-            BS_TR_ADD(0);
-            if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
-            BS_TR_ADD(1);
-            if (ok) {
-              tc_fence_after();
-              const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * 256 + wg * 128);
-              uint32_t v[64];
-              tmem_ld64(tbase, v);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) ffma2(acc[i], v[2 * i], v[2 * i + 1], sc2);
-              tmem_ld64(tbase + 64, v);
-              tmem_ld_wait();
-              // Everything this warp needs from the partial buffer is in registers: hand it back
-              // to the MMA issuer before the second half of the FMAs.
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&pempty[b]);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
-              BS_TR_ADD(2);
-            }
-            if (++b == 2) {
-              b = 0;
-              pph ^= 1;
-            }
-          }
+          for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
+        }
+        if (++b == 2) {
+          b = 0;
+          pph ^= 1;
         }
       }
 
