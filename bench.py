@@ -285,10 +285,13 @@ def run_ours(args, rank, world, device) -> dict | None:
     if rank != 0:
         return None
     fused_tflops = 2.0 * M_PREFILL * n2_local * HIDDEN / (fused_ms * 1e-3) / 1e12
-    traffic = None
-    tfile = ROOT / "profiles" / "traffic.json"
+    traffic = None  # DRAM bytes per launch of the dominant kernel, from one ncu capture (profiles/)
+    tfile = ROOT / "profiles" / "traffic.txt"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get(f"fused_prefill_tp{world}")
+        for line in tfile.read_text().splitlines():
+            key, _, val = line.partition(":")
+            if key.strip() == f"fused_prefill_tp{world}" and val.strip():
+                traffic = int(val.strip())
     res = {
         "metric": METRIC,
         "value": round(tflops, 1),

@@ -158,13 +158,16 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
+      BS_TR_DECL(1);
       for (long long u = u0; u < u1; ++u) {
         const int t = static_cast<int>(u / KB);
         const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
+        BS_TR_MARK();
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) {
           ok = false;
           break;
         }
+        BS_TR_ADD(0);
         uint8_t* st = smem + s * Cfg::kStageBytes;
         mbar_arrive_expect_tx(&full[s], Cfg::kWBytes + Cfg::kXBytes);
 #pragma unroll
@@ -178,6 +181,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           ph ^= 1;
         }
       }
+      BS_TR_FLUSH(0, 1);
       if (!ok) {
         for (int i = 0; i < S; ++i)
           if (issued & (1u << i))
@@ -190,10 +194,13 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
       constexpr uint32_t idesc = idesc_e4m3_f32(128, NTP);
       int s = 0, b = 0;
       uint32_t ph = 0, pph = 0;
+      BS_TR_DECL(2);
       for (long long u = u0; u < u1; ++u) {
-        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull) ||
-            !mbar_wait(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty))
-          break;
+        BS_TR_MARK();
+        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) break;
+        BS_TR_ADD(0);
+        if (!mbar_wait(&pempty[b], pph ^ 1, abort_flag, p.status, kErrTimeoutPEmpty)) break;
+        BS_TR_ADD(1);
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * Cfg::kStageBytes);
         const uint32_t xs = st + Cfg::kWBytes;
@@ -216,6 +223,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           pph ^= 1;
         }
       }
+      BS_TR_FLUSH(4, 2);
       mma_commit(drain);
       mbar_wait(drain, 0, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
     }
@@ -268,15 +276,19 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
     int seg_kb0 = static_cast<int>(u0 % KB);
     constexpr int G0 = NTP < 64 ? NTP : 64;         // first column group
     constexpr int G1 = NTP - G0;                    // second column group (NTP > 64)
+    BS_TR_DECL(4);
     auto unit_body = [&](long long u, ScalePair& nxt) {
       const int t = static_cast<int>(u / KB);
       const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
       const int slot_next = slot == 2 ? 0 : slot + 1;
+      BS_TR_MARK();
       if (r < NTP) ring[(slot_next * NWG + wg) * NTP + r] = scale_value(nxt);
       nxt = load_scales(u + 3);
       named_bar_sync(1, NPROMO);
+      BS_TR_ADD(0);
 
       if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
+      BS_TR_ADD(1);
       if (ok) {
         tc_fence_after();
         const uint32_t tbase = tmem + lane_addr + static_cast<uint32_t>(b * NWG * NTP + wg * NTP);
@@ -307,6 +319,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           }
         }
       }
+      BS_TR_ADD(2);
       if (++b == 2) {
         b = 0;
         pph ^= 1;
@@ -430,12 +443,14 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < NTP / 2; ++i) acc[i] = 0;
         seg_kb0 = 0;
+        BS_TR_ADD(3);
       }
     };
     for (long long u = u0; u < u1; u += 2) {
       unit_body(u, nxt_a);
       if (u + 1 < u1) unit_body(u + 1, nxt_b);
     }
+    if (lane == 0 && q == 0) BS_TR_FLUSH(8, 4);
   }
 
   // ------------------------------------------------------------ teardown
