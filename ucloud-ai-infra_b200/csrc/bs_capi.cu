@@ -99,8 +99,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int ntp_for(int M) { return ((M + 15) / 16) * 16; }
 
-// Grid of the decode kernels: one CTA per SM, never more CTAs than (tile, K block) units.
+// Grid of the decode kernels. When the weight tiles nearly match the SM count (>= 90%), one CTA
+// per tile streams whole tiles and no tile is split (no partial sums, no finishing CTA);
+// otherwise the stream-K split over one CTA per SM keeps every SM streaming equal bytes. Never
+// more CTAs than (tile, K block) units.
 int decode_grid(int num_sms, int tiles, int KB) {
+  if (tiles <= num_sms && 10 * tiles >= 9 * num_sms) return tiles;
   const long long units = static_cast<long long>(tiles) * KB;
   return static_cast<int>(units < num_sms ? units : num_sms);
 }
@@ -204,7 +208,12 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   p.ldc = fused ? N / 2 : ldc;
   p.b_tiled = b_tiled;
   p.out_f32 = fused ? 0 : out_dtype;
-  p.group_m = 16;
+  // Prefill raster: all M tiles in one group when that A panel stays in L2 (each weight tile is
+  // then read from HBM once), else 16 M tiles per group.
+  {
+    const long long a_panel = static_cast<long long>(M) * K;
+    p.group_m = a_panel <= (48ll << 20) ? (M + 127) / 128 : 16;
+  }
   p.As = As;
   p.Bs = Bs;
   p.out = out;
