@@ -34,6 +34,7 @@ extern "C" {
 #define BS_ERR_TMAP 4         /* cuTensorMapEncodeTiled is unavailable or rejected the tensor  */
 #define BS_ERR_CUDA 5         /* a CUDA runtime call failed (launch, attribute, device query)  */
 #define BS_ERR_BUILD 6        /* a kernel's register count does not match its setmaxnreg split */
+#define BS_ERR_SCRATCH 7      /* bs_fp8_gemm_noalloc: the shape needs more than its fixed scratch   */
 #define BS_ERR_TIMEOUT_FULL 101     /* device status: bounded wait on a TMA stage ran out       */
 #define BS_ERR_TIMEOUT_EMPTY 102    /* device status: bounded wait for a free stage ran out     */
 #define BS_ERR_TIMEOUT_PFULL 103    /* device status: bounded wait for an MMA partial ran out   */
@@ -64,6 +65,19 @@ int bs_fp8_gemm(const void* A, const void* B, void* C, const float* As, const fl
 int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* As, const float* Bs, float* Qs,
                            int M, int N2, int K, int b_tiled, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* Allocation-free variant of bs_fp8_gemm, for callers that cannot call cudaMalloc (an engine that
+ * reserves all device memory up front, an embedding whose only allocator is its own arena, a
+ * thread that must not block on the driver's allocator). No counterpart in the reference.
+ * Same arguments and results as bs_fp8_gemm without the workspace: decode shapes (M <= 128) use
+ * a fixed 4 MiB scratch array inside the library (held on every GPU that loads it until exit);
+ * a shape whose split-K scratch would exceed it returns BS_ERR_SCRATCH. The first call on a
+ * device looks up that array's device address, so make it before any stream capture. Every call
+ * shares the array: calls that overlap on the GPU (different streams, or concurrent host
+ * threads) race on it. It allocates nothing (no cudaMalloc/cudaFree); it clears the array's
+ * counter words with cudaMemsetAsync on `stream` before each launch. */
+int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N,
+                        int K, int ldc, int b_tiled, int out_dtype, void* stream);
 
 /* Workspace bytes the decode kernels need for (M, N, K); 0 when M > 128 or M == 0. */
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused);

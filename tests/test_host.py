@@ -43,7 +43,7 @@ def test_binding_covers_header():
 
 def test_abi_version_and_error_strings(lib):
     assert lib.bs_fp8_abi_version() == 1
-    for code in (0, 1, 2, 3, 4, 5, 6, 101, 102, 103, 104, 105, 199):
+    for code in (0, 1, 2, 3, 4, 5, 6, 7, 101, 102, 103, 104, 105, 199):
         text = lib.bs_fp8_error_string(code).decode()
         assert text and text != "unknown status code"
     assert lib.bs_fp8_error_string(12345).decode() == "unknown status code"
@@ -67,15 +67,29 @@ def test_argument_validation_needs_no_gpu(lib):
     assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
 
 
+def _decode_grid(sms, tiles, kb):
+    """One CTA per tile when tiles nearly match the SMs (>= 90%), else one CTA per SM (stream-K)."""
+    if tiles <= sms and 10 * tiles >= 9 * sms:
+        return tiles
+    return min(sms, tiles * kb)
+
+
+def _decode_ws(M, N, K, fused, sms):
+    tiles = N // 256 if fused else N // 128
+    ntp = (M + 15) // 16 * 16
+    counters = (tiles * 4 + 255) // 256 * 256
+    return counters + _decode_grid(sms, tiles, K // 128) * 2 * (2 if fused else 1) * ntp * 128 * 4
+
+
 def test_workspace_size_formula(lib):
     # decode shapes need counters + G * 2 * nwg * ntp * 128 floats; prefill shapes need none
     assert lib.bs_fp8_workspace_bytes(129, 256, 256, 0) == 0
     assert lib.bs_fp8_workspace_bytes(0, 256, 256, 0) == 0
-    w1 = lib.bs_fp8_workspace_bytes(1, 34816, 5120, 1)
-    w112 = lib.bs_fp8_workspace_bytes(112, 34816, 5120, 1)
-    assert 0 < w1 < w112
     sms = lib.bs_fp8_num_sms() or 148
-    assert w112 == 256 + sms * 2 * 2 * 112 * 128 * 4 + (136 * 4 + 255) // 256 * 256 - 256
+    for M, N, K, fused in [(1, 34816, 5120, 1), (112, 34816, 5120, 1), (128, 6144, 5120, 0), (5, 384, 17408, 0),
+                           (3, 128, 256, 0)]:
+        assert lib.bs_fp8_workspace_bytes(M, N, K, fused) == _decode_ws(M, N, K, fused, sms), (M, N, K, fused)
+    assert lib.bs_fp8_workspace_bytes(1, 34816, 5120, 1) < lib.bs_fp8_workspace_bytes(112, 34816, 5120, 1)
 
 
 def _fresh_module(monkeypatch, **env):

@@ -246,6 +246,39 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
                : launch_prefill<false>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
 }
 
+// ------------------------------------------------------------ allocation-free GEMM entry point
+// Some callers cannot call cudaMalloc: an engine that reserves all device memory up front and
+// forbids allocations afterwards, an embedding whose only allocator is its own arena, or a host
+// thread that must never block on the driver's allocator. bs_fp8_gemm_noalloc serves them: the
+// decode kernel's split-K scratch (per-tile arrival counters and fp32 partial tiles) lives in
+// this fixed array, which every GPU that loads the library holds until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB: counters + partial tiles
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device memory, so the kernel
+// gets the array's device address, looked up once per device (with that device current).
+struct NoAllocScratch {
+  std::once_flag once[kMaxDevices];
+  void* ptr[kMaxDevices] = {};
+  int rc[kMaxDevices] = {};
+};
+NoAllocScratch g_noalloc;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  const cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) return cuda_fail(e0, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return BS_ERR_CUDA;
+  std::call_once(g_noalloc.once[dev], [dev] {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc.rc[dev] = e == cudaSuccess ? BS_OK : cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc.ptr[dev] = p;
+  });
+  *out = g_noalloc.ptr[dev];
+  return g_noalloc.rc[dev];
+}
+
 __global__ void k_selftest_wait(uint64_t limit_ns, int* status) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -273,6 +306,29 @@ int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* A
                            int M, int N2, int K, int b_tiled, void* workspace, size_t workspace_bytes,
                            void* stream) {
   return run_gemm(true, A, B, Q, As, Bs, Qs, M, N2, K, N2 / 2, b_tiled, 0, workspace, workspace_bytes, stream);
+}
+
+int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
+                        int ldc, int b_tiled, int out_dtype, void* stream) {
+  // Shapes above 128 rows run the prefill kernel, which needs no scratch; decode shapes use the
+  // static array, and are refused when their scratch would not fit in it.
+  if (M <= 128 && M > 0 && N > 0 && K > 0 && K % 128 == 0 && N % 128 == 0) {
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != BS_OK) return rc;
+    DeviceState* d = device_state();
+    if (!d) return BS_ERR_CUDA;
+    const int tiles = N / 128;
+    const size_t need = decode_ws_bytes(decode_grid(d->num_sms, tiles, K / 128), 1, ntp_for(M), tiles);
+    if (need > kNoAllocScratchBytes) return BS_ERR_SCRATCH;
+    // The array keeps the previous call's contents; the counters must start at zero.
+    const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc counters)");
+    return run_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype, scratch,
+                    kNoAllocScratchBytes, stream);
+  }
+  return run_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype, nullptr, 0, stream);
 }
 
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {
@@ -350,6 +406,7 @@ const char* bs_fp8_error_string(int code) {
     case BS_ERR_TMAP: return "TMA descriptor could not be created";
     case BS_ERR_CUDA: return "CUDA runtime call failed";
     case BS_ERR_BUILD: return "kernel register count does not match its setmaxnreg split; refusing to launch";
+    case BS_ERR_SCRATCH: return "shape needs more split-K scratch than bs_fp8_gemm_noalloc's fixed 4 MiB array";
     case BS_ERR_TIMEOUT_FULL: return "device: bounded wait for a TMA stage ran out";
     case BS_ERR_TIMEOUT_EMPTY: return "device: bounded wait for a free stage ran out";
     case BS_ERR_TIMEOUT_PFULL: return "device: bounded wait for an MMA partial ran out";
