@@ -26,6 +26,8 @@
 // each gate thread owns a whole 128-wide quant group of its row:
 //   y = silu(g) * u;  scale = max(amax|y|, 1e-10) / 448;  q = sat_e4m3(y * (1 / scale)).
 #pragma once
+#include <type_traits>
+
 #include "bs_common.cuh"
 
 namespace bs {
@@ -53,7 +55,7 @@ struct PrefillCfg {
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = 256 * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 : 0;
+  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 + 128 * 2 * 4 : 0;  // half groups + amax halves
   static constexpr int kBarOff = kStages * kStageBytes + kXchBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers, then slack for 1 KB alignment
   static constexpr int kTmemCols = 512;
@@ -310,49 +312,72 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
           }
         }
       } else {
-        // Up accumulators cross to the gate warps. 16-byte chunks are XOR-swizzled by row so
-        // that the 8 rows of one store phase hit 8 different bank groups.
+        // The 128-wide quant group of row r is split between the two warpgroups: the gate
+        // thread finishes columns 0-63 and the up thread columns 64-127. Each hands the other
+        // the half it lacks through shared memory (the up thread its u[0:64), the gate thread its
+        // g[64:128)), and the two agree on the group's amax through amax_x. 16-byte chunks are
+        // XOR-swizzled by row so the 8 rows of one store phase hit 8 different bank groups; the
+        // swizzle keeps chunks 0-15 (u half) and 16-31 (g half) apart.
         float4* x4 = reinterpret_cast<float4*>(xch);
-        if (wg == 1) {
+        float* amax_x = xch + 128 * 128;
+        // Accumulator indices must be compile-time constants (a runtime index would move the
+        // whole array to local memory), so each warpgroup runs its own instance of the steps.
+        auto finish_half = [&](auto is_up) {
+          constexpr bool kUp = decltype(is_up)::value;
+          constexpr int give = kUp ? 0 : 32;   // first pair handed to the other warpgroup
+          constexpr int keep = kUp ? 32 : 0;   // first pair finished here
+          constexpr int c4_give = kUp ? 0 : 16;
+          constexpr int c4_take = kUp ? 16 : 0;
 #pragma unroll
-          for (int c4 = 0; c4 < 32; ++c4)
-            x4[r * 32 + (c4 ^ (r & 7))] =
-                make_float4(lo_f(acc[2 * c4]), hi_f(acc[2 * c4]), lo_f(acc[2 * c4 + 1]), hi_f(acc[2 * c4 + 1]));
-        }
-        named_bar_sync(1, 256);
-        if (wg == 0) {
+          for (int j = 0; j < 16; ++j) {
+            const int c4 = c4_give + j;
+            x4[r * 32 + (c4 ^ (r & 7))] = make_float4(lo_f(acc[give + 2 * j]), hi_f(acc[give + 2 * j]),
+                                                      lo_f(acc[give + 2 * j + 1]), hi_f(acc[give + 2 * j + 1]));
+          }
+          named_bar_sync(1, 256);
           float amax = 0.f;
 #pragma unroll
-          for (int c4 = 0; c4 < 32; ++c4) {
-            const float4 u = x4[r * 32 + (c4 ^ (r & 7))];
-            const float y0 = silu_mul(lo_f(acc[2 * c4]), u.x);
-            const float y1 = silu_mul(hi_f(acc[2 * c4]), u.y);
-            const float y2 = silu_mul(lo_f(acc[2 * c4 + 1]), u.z);
-            const float y3 = silu_mul(hi_f(acc[2 * c4 + 1]), u.w);
-            acc[2 * c4] = pack_f2(y0, y1);
-            acc[2 * c4 + 1] = pack_f2(y2, y3);
+          for (int j = 0; j < 16; ++j) {
+            const int c4 = c4_take + j;
+            const float4 o = x4[r * 32 + (c4 ^ (r & 7))];
+            const int e = keep + 2 * j;
+            const float a0 = lo_f(acc[e]), a1 = hi_f(acc[e]), a2 = lo_f(acc[e + 1]), a3 = hi_f(acc[e + 1]);
+            // gate thread: g = own, u = other; up thread: g = other, u = own
+            const float y0 = kUp ? silu_mul(o.x, a0) : silu_mul(a0, o.x);
+            const float y1 = kUp ? silu_mul(o.y, a1) : silu_mul(a1, o.y);
+            const float y2 = kUp ? silu_mul(o.z, a2) : silu_mul(a2, o.z);
+            const float y3 = kUp ? silu_mul(o.w, a3) : silu_mul(a3, o.w);
+            acc[e] = pack_f2(y0, y1);
+            acc[e + 1] = pack_f2(y2, y3);
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
           }
+          amax_x[r * 2 + (kUp ? 1 : 0)] = amax;
+          named_bar_sync(1, 256);
+          amax = fmaxf(amax_x[r * 2], amax_x[r * 2 + 1]);
           const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
           const float inv = __fdiv_rn(1.0f, scale);
           if (ok && row_ok) {
             const int I = I_blk * 128;
-            p.qs[static_cast<size_t>(row) * I_blk + tn] = scale;
+            if (!kUp) p.qs[static_cast<size_t>(row) * I_blk + tn] = scale;
             uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * I +
-                                                  static_cast<size_t>(tn) * 128);
+                                                  static_cast<size_t>(tn) * 128 + (kUp ? 64 : 0));
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 4; ++j) {
               uint32_t w[4];
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
-                const int e = 8 * j + 2 * h;  // pair index: columns 16j + 4h .. +3
+                const int e = keep + 8 * j + 2 * h;  // pair index: columns 16j + 4h .. +3 of this half
                 w[h] = f2_to_e4m3x2(__fmul_rn(lo_f(acc[e]), inv), __fmul_rn(hi_f(acc[e]), inv)) |
                        (f2_to_e4m3x2(__fmul_rn(lo_f(acc[e + 1]), inv), __fmul_rn(hi_f(acc[e + 1]), inv)) << 16);
               }
               dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
             }
           }
-        }
+        };
+        if (wg == 0)
+          finish_half(std::false_type{});
+        else
+          finish_half(std::true_type{});
         named_bar_sync(1, 256);
       }
       BS_TR_ADD(3);
