@@ -239,21 +239,47 @@ def run_ours(args, rank, world, device) -> dict | None:
     tflops = mlp_flops(M_PREFILL) / (ms * 1e-3) / 1e12
     assert torch.isfinite(out.float()).all().item(), "non-finite MLP output"
 
-    # e2e: pinned host input -> device -> MLP -> pinned host output, inside the timed region.
+    # e2e: every step copies its input from pinned host memory to the device, runs the MLP through
+    # the public API and copies the result back to pinned host memory, all inside the timed region.
+    # Copies run on their own streams with two device buffers each way, so step i's upload and
+    # step i-1's download overlap step i's compute (the usual serving pipeline); the timed region
+    # spans from the first upload to the last download.
     xh = x.cpu().pin_memory()
     oh = torch.empty(M_PREFILL, HIDDEN, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
-    for _ in range(2):
-        xd.copy_(xh, non_blocking=True)
-        oh.copy_(step(xd), non_blocking=True)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    xd = [torch.empty_like(x) for _ in range(2)]
+    od = [torch.empty(M_PREFILL, HIDDEN, dtype=torch.bfloat16, device=device) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def pipelined(nsteps, e_start=None, e_end=None):
+        if e_start is not None:
+            e_start.record(s_in)
+        for i in range(nsteps):
+            j = i % 2
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(ev_done[j])      # compute of step i-2 no longer reads xd[j]
+                xd[j].copy_(xh, non_blocking=True)
+                ev_in[j].record(s_in)
+            stream.wait_event(ev_in[j])
+            if i >= 2:
+                stream.wait_event(ev_out[j])         # download of step i-2 finished with od[j]
+            od[j].copy_(step(xd[j]))
+            ev_done[j].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[j])
+                oh.copy_(od[j], non_blocking=True)
+                ev_out[j].record(s_out)
+        if e_end is not None:
+            e_end.record(s_out)
+
+    pipelined(2)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        xd.copy_(xh, non_blocking=True)
-        oh.copy_(step(xd), non_blocking=True)
-    e1.record(stream)
+    pipelined(args.steps, e0, e1)
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
@@ -363,7 +389,7 @@ class CpuReference:
         return time.perf_counter() - t, mlp_flops(rows)
 
 
-def cpu_baseline_sample(rows: int, reps: int = 1) -> dict:
+def cpu_baseline_sample(rows: int, reps: int = 3) -> dict:
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ref = CpuReference()
