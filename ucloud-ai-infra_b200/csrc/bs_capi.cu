@@ -73,9 +73,10 @@ DeviceState* device_state() {
   return d->err ? nullptr : d;
 }
 
-// 2-D uint8 tensor map with a 128-byte-swizzled box; out-of-range elements read as zero.
+// 2-D uint8 tensor map with a 128-byte-swizzled box (operand loads) or a plain box (stores of
+// row-major tiles); out-of-range elements read as zero and are never written.
 int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
-             uint32_t box_outer) {
+             uint32_t box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = encoder();
   if (!enc) return BS_ERR_TMAP;
   cuuint64_t dims[2] = {inner, outer};
@@ -83,7 +84,7 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, u
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BS_OK : BS_ERR_TMAP;
 }
@@ -145,29 +146,29 @@ int prepare_kernel(int smem_bytes, int launch_regs) {
 }
 
 template <bool FUSED, int NTP>
-int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const bs::GemmParams& p, int grid,
-                  cudaStream_t s) {
+int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmO, const bs::GemmParams& p,
+                  int grid, cudaStream_t s) {
   using Cfg = bs::DecodeCfg<FUSED, NTP>;
   constexpr auto kern = bs::k_decode<FUSED, NTP>;
   const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::kLaunchRegs);
   if (rc != BS_OK) return rc;
   cudaGetLastError();  // clear an older error so the check below sees this launch only
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmW, tmX, p);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmW, tmX, tmO, p);
   return launch_status("k_decode launch");
 }
 
 template <bool FUSED>
-int dispatch_decode(int ntp, const CUtensorMap& tmW, const CUtensorMap& tmX, const bs::GemmParams& p, int grid,
-                    cudaStream_t s) {
+int dispatch_decode(int ntp, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmO,
+                    const bs::GemmParams& p, int grid, cudaStream_t s) {
   switch (ntp) {
-    case 16: return launch_decode<FUSED, 16>(tmW, tmX, p, grid, s);
-    case 32: return launch_decode<FUSED, 32>(tmW, tmX, p, grid, s);
-    case 48: return launch_decode<FUSED, 48>(tmW, tmX, p, grid, s);
-    case 64: return launch_decode<FUSED, 64>(tmW, tmX, p, grid, s);
-    case 80: return launch_decode<FUSED, 80>(tmW, tmX, p, grid, s);
-    case 96: return launch_decode<FUSED, 96>(tmW, tmX, p, grid, s);
-    case 112: return launch_decode<FUSED, 112>(tmW, tmX, p, grid, s);
-    case 128: return launch_decode<FUSED, 128>(tmW, tmX, p, grid, s);
+    case 16: return launch_decode<FUSED, 16>(tmW, tmX, tmO, p, grid, s);
+    case 32: return launch_decode<FUSED, 32>(tmW, tmX, tmO, p, grid, s);
+    case 48: return launch_decode<FUSED, 48>(tmW, tmX, tmO, p, grid, s);
+    case 64: return launch_decode<FUSED, 64>(tmW, tmX, tmO, p, grid, s);
+    case 80: return launch_decode<FUSED, 80>(tmW, tmX, tmO, p, grid, s);
+    case 96: return launch_decode<FUSED, 96>(tmW, tmX, tmO, p, grid, s);
+    case 112: return launch_decode<FUSED, 112>(tmW, tmX, tmO, p, grid, s);
+    case 128: return launch_decode<FUSED, 128>(tmW, tmX, tmO, p, grid, s);
     default: return BS_ERR_ARG;
   }
 }
@@ -228,6 +229,8 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
     const int nwg = fused ? 2 : 1;
     const int tiles = fused ? N / 256 : N / 128;
     const int grid = decode_grid(d->num_sms, tiles, K / 128);
+    // the kernel indexes (tile, K block) units with 32-bit products unit * grid
+    if (static_cast<long long>(tiles) * (K / 128) * grid >= (1ll << 31)) return BS_ERR_ARG;
     const size_t need = decode_ws_bytes(grid, nwg, ntp, tiles);
     if (!ws || ws_bytes < need || !aligned16(ws)) return BS_ERR_WORKSPACE;
     const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
@@ -235,7 +238,11 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + counters);
     CUtensorMap tmX;
     if (make_map(&tmX, A, K, M, K, 128, ntp) != BS_OK) return BS_ERR_TMAP;
-    return fused ? dispatch_decode<true>(ntp, tmB, tmX, p, grid, s) : dispatch_decode<false>(ntp, tmB, tmX, p, grid, s);
+    if (!fused) return dispatch_decode<false>(ntp, tmB, tmX, tmX, p, grid, s);
+    // fused: the quantised output Q [M, I] is written tile by tile with TMA stores
+    CUtensorMap tmO;
+    if (make_map(&tmO, out, N / 2, M, N / 2, 128, ntp, CU_TENSOR_MAP_SWIZZLE_NONE) != BS_OK) return BS_ERR_TMAP;
+    return dispatch_decode<true>(ntp, tmB, tmX, tmO, p, grid, s);
   }
 
   CUtensorMap tmA;

@@ -139,6 +139,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2-D tiled store of one box from shared memory (rows outside the tensor are not written),
+// tracked by the issuing thread's bulk async-group. Generic-proxy writes to `src` must be
+// followed by fence_proxy_async_smem() and a barrier before the store is issued.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Returns once every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -236,6 +252,40 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Issues loads of N consecutive TMEM columns (N a multiple of 4, at most 128) of this warp's 32
+// lanes into v[0..N), largest pieces first, all in flight together; the caller waits once.
+template <int N, int OFF = 0>
+__device__ __forceinline__ void tmem_ld_run(uint32_t taddr, uint32_t* v) {
+  static_assert(N % 4 == 0 && N >= 0, "column run");
+  if constexpr (N >= 64) {
+    tmem_ld64(taddr + OFF, *reinterpret_cast<uint32_t(*)[64]>(v + OFF));
+    tmem_ld_run<N - 64, OFF + 64>(taddr, v);
+  } else if constexpr (N >= 32) {
+    tmem_ld32(taddr + OFF, *reinterpret_cast<uint32_t(*)[32]>(v + OFF));
+    tmem_ld_run<N - 32, OFF + 32>(taddr, v);
+  } else if constexpr (N >= 16) {
+    tmem_ld16(taddr + OFF, *reinterpret_cast<uint32_t(*)[16]>(v + OFF));
+    tmem_ld_run<N - 16, OFF + 16>(taddr, v);
+  } else if constexpr (N >= 8) {
+    tmem_ld8(taddr + OFF, *reinterpret_cast<uint32_t(*)[8]>(v + OFF));
+    tmem_ld_run<N - 8, OFF + 8>(taddr, v);
+  } else if constexpr (N >= 4) {
+    tmem_ld4(taddr + OFF, *reinterpret_cast<uint32_t(*)[4]>(v + OFF));
+  }
 }
 
 // Shared-memory matrix descriptor of a K-major operand laid out by TMA with 128-byte swizzle:
@@ -368,6 +418,51 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // the fast divide returns 0, the correct limit.
 __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(__fdividef(g, 1.0f + __expf(-g)), u);
+}
+
+// ---------------------------------------------------------------- warp max of N values per lane
+// Max over the 32 lanes of each of v[0..N) (unsigned; non-negative floats order like their bits).
+// While the count is even, each exchange halves it: the lanes with bit OFF set keep the upper half
+// of the values and send the lower half to their partner, so N values cost N/2 + N/4 + ...
+// shuffles instead of 5*N. An odd remainder finishes with plain xor reductions. Afterwards lane
+// L holds the maxima of tokens warp_max_base<N, 16>(L) + [0, warp_max_count<N, 16>()), and the
+// lanes that differ only in bits of warp_max_dup_mask<N, 16>() hold identical copies.
+template <int N, int OFF>
+__device__ __forceinline__ void warp_max_halving(uint32_t* v, int lane) {
+  if constexpr (OFF > 0) {
+    if constexpr (N % 2 == 0) {
+      const bool upper = (lane & OFF) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+        const uint32_t send = upper ? v[i] : v[N / 2 + i];
+        const uint32_t keep = upper ? v[N / 2 + i] : v[i];
+        v[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, OFF));
+      }
+      warp_max_halving<N / 2, OFF / 2>(v, lane);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = max(v[i], __shfl_xor_sync(0xffffffffu, v[i], OFF));
+      warp_max_halving<N, OFF / 2>(v, lane);
+    }
+  }
+}
+template <int N, int OFF>
+__host__ __device__ constexpr int warp_max_count() {
+  if constexpr (OFF == 0) return N;
+  else if constexpr (N % 2 == 0) return warp_max_count<N / 2, OFF / 2>();
+  else return warp_max_count<N, OFF / 2>();
+}
+template <int N, int OFF>
+__host__ __device__ constexpr int warp_max_dup_mask() {
+  if constexpr (OFF == 0) return 0;
+  else if constexpr (N % 2 == 0) return warp_max_dup_mask<N / 2, OFF / 2>();
+  else return OFF | warp_max_dup_mask<N, OFF / 2>();
+}
+template <int N, int OFF>
+__device__ __forceinline__ int warp_max_base(int lane) {
+  if constexpr (OFF == 0) return 0;
+  else if constexpr (N % 2 == 0) return ((lane & OFF) ? N / 2 : 0) + warp_max_base<N / 2, OFF / 2>(lane);
+  else return warp_max_base<N, OFF / 2>(lane);
 }
 
 }  // namespace bs
