@@ -187,16 +187,17 @@ def build_mlp(rank, world, device):
                                      sglang_compat.Fp8BlockLinear(dn_q, dn_s))
         fp8_hand_sm100.relayout(mlp)
         assert getattr(mlp.gate_up_proj.weight, "tiles", None) is not None, "relayout did not run"
-        return mlp, (mlp.gate_up_proj.weight.tiles, gu_s), 2 * INTER
+        return (mlp, (mlp.gate_up_proj.weight.tiles, gu_s), (mlp.down_proj.weight.tiles, dn_s), 2 * INTER)
     shard = tp.make_shard(gu_q, gu_s, dn_q, dn_s, rank, world, device=device, tiled=True)
     del gu_q, dn_q
-    return tp.TensorParallelMLP(shard), (shard.gate_up, shard.gate_up_scale), 2 * INTER // world
+    return (tp.TensorParallelMLP(shard), (shard.gate_up, shard.gate_up_scale), (shard.down, shard.down_scale),
+            2 * INTER // world)
 
 
 def run_ours(args, rank, world, device) -> dict | None:
     from fp8_hand_b200 import ops
     torch.cuda.set_device(device)
-    mlp, (gu_tiles, gu_s), n2_local = build_mlp(rank, world, device)
+    mlp, (gu_tiles, gu_s), (dn_tiles, dn_s), n2_local = build_mlp(rank, world, device)
     x = make_x(M_PREFILL, device)
     stream = torch.cuda.current_stream(device)
 
@@ -285,27 +286,48 @@ def run_ours(args, rank, world, device) -> dict | None:
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
     clk.__exit__(None, None, None)
 
-    # Decode / verify sizes: fused gate_up (config 2) on this rank's shard, HBM GB/s.
-    decode = {}
+    # Decode / verify sizes on this rank's shard, HBM GB/s: fused gate_up (config 2) and the
+    # down_proj GEMM. A decode step is served from a captured CUDA graph, so each size is timed as a
+    # graph of `reps` back-to-back calls (host launch overhead excluded), max over ranks.
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
+    reps = 50
+
+    def graph_us(fn):
+        side = torch.cuda.Stream(device)
+        with torch.cuda.stream(side):
+            for _ in range(3):  # also sizes this stream's decode workspace before capture
+                fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        g.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return max_over_ranks(s.elapsed_time(e) / reps, world, device) * 1e3
+
+    decode, decode_down = {}, {}
+    n_down = dn_tiles.shape[0] * 128
     for M in DECODE_MS:
         xm = make_x(M, device, seed=2, outlier_frac=0.0)
         A, As = ops.group_quant(xm)
-        for _ in range(5):
-            ops.gemm_silu_quant(A, gu_tiles, As, gu_s, b_tiled=True)
-        torch.cuda.synchronize()
-        barrier(world)
-        reps = 50
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(reps):
-            ops.gemm_silu_quant(A, gu_tiles, As, gu_s, b_tiled=True)
-        e.record(stream)
-        torch.cuda.synchronize()
-        dms = max_over_ranks(s.elapsed_time(e) / reps, world, device)
-        gbs = fused_bytes(M, n2_local) / (dms * 1e-3) / 1e9
-        decode[str(M)] = {"us": round(dms * 1e3, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+        us = graph_us(lambda: ops.gemm_silu_quant(A, gu_tiles, As, gu_s, b_tiled=True))
+        gbs = fused_bytes(M, n2_local) / (us * 1e-6) / 1e9
+        decode[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+        Q, Qs = ops.gemm_silu_quant(A, gu_tiles, As, gu_s, b_tiled=True)
+        yd = torch.empty(M, n_down, dtype=torch.bfloat16, device=device)
+        us = graph_us(lambda: ops.gemm(Q, dn_tiles, Qs, dn_s, b_tiled=True, out=yd))
+        k_down = Q.shape[1]
+        gbs = (n_down * k_down + M * k_down * (1 + 4 / 128) + 2 * M * n_down) / (us * 1e-6) / 1e9
+        decode_down[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
 
     fp8_peak = fp8_peak_tflops(device) if rank == 0 else None
     if rank != 0:
@@ -348,7 +370,9 @@ def run_ours(args, rank, world, device) -> dict | None:
             "traffic": traffic,
         },
         "decode_fused_gate_up": {"unit": "GB/s", "hbm_peak_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
-                                 "by_M": decode},
+                                 "timing": f"CUDA graph of {reps} back-to-back calls", "by_M": decode},
+        "decode_down_proj": {"unit": "GB/s", "hbm_peak_gbs": hbm, "timing": f"CUDA graph of {reps} back-to-back calls",
+                             "by_M": decode_down},
         "e2e": {"value": round(mlp_flops(M_PREFILL) / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": xh.numel() * xh.element_size(),

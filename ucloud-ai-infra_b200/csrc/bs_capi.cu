@@ -1,6 +1,7 @@
 // C-ABI entry points of libbs_fp8_sm100.so: argument checks, TMA descriptor creation, kernel
 // selection and launch. One translation unit so that every kernel can name the status word.
 #include <mutex>
+#include <utility>
 #include <cstdio>
 #include <cstring>
 
@@ -145,6 +146,28 @@ int prepare_kernel(int smem_bytes, int launch_regs) {
   return st.rc[dev];
 }
 
+// Launches a library kernel as a programmatic dependent launch: it may begin while the previous
+// kernel on the stream is still running, and its threads wait (griddepcontrol.wait) before any
+// global access that could depend on that kernel.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), int grid, int block, int smem, cudaStream_t s, const char* where,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaGetLastError();  // clear an older error so the check below sees this launch only
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, where);
+  return launch_status(where);
+}
+
 template <bool FUSED, int NTP>
 int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmO, const bs::GemmParams& p,
                   int grid, cudaStream_t s) {
@@ -152,9 +175,7 @@ int launch_decode(const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensor
   constexpr auto kern = bs::k_decode<FUSED, NTP>;
   const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::kLaunchRegs);
   if (rc != BS_OK) return rc;
-  cudaGetLastError();  // clear an older error so the check below sees this launch only
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmW, tmX, tmO, p);
-  return launch_status("k_decode launch");
+  return launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, s, "k_decode launch", tmW, tmX, tmO, p);
 }
 
 template <bool FUSED>
@@ -181,9 +202,7 @@ int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::Gem
   const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::Regs::kLaunch);
   if (rc != BS_OK) return rc;
   const int grid = num_tiles < num_sms ? num_tiles : num_sms;
-  cudaGetLastError();
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(tmA, tmB, p);
-  return launch_status("k_prefill launch");
+  return launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, s, "k_prefill launch", tmA, tmB, p);
 }
 
 // Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant.
@@ -358,10 +377,9 @@ int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K,
   long long blocks = (groups + per_block - 1) / per_block;
   const long long cap = static_cast<long long>(d->num_sms) * 16;
   if (blocks > cap) blocks = cap;
-  cudaGetLastError();
-  bs::k_group_quant<<<static_cast<int>(blocks), bs::kQuantThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<uint8_t*>(A), As, M, K);
-  return launch_status("k_group_quant launch");
+  return launch_pdl(bs::k_group_quant, static_cast<int>(blocks), bs::kQuantThreads, 0, static_cast<cudaStream_t>(stream),
+                    "k_group_quant launch", static_cast<const __nv_bfloat16*>(x), ldx, static_cast<uint8_t*>(A), As,
+                    M, K);
 }
 
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {

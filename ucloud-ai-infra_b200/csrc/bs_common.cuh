@@ -139,6 +139,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Brings one box of a tensor into L2 without waiting for it (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+// Programmatic dependent launch. Every library kernel is launched allowed to start before the
+// previous kernel on its stream has finished; grid_dep_wait() returns once the grids it depends on
+// have completed and their writes are visible, so every global access of a thread that could
+// depend on them comes after it (an L2 prefetch cannot observe stale data and may precede it).
+// grid_dep_launch() lets the next such launch start its prologue on SMs this grid leaves free.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 2-D tiled store of one box from shared memory (rows outside the tensor are not written),
 // tracked by the issuing thread's bulk async-group. Generic-proxy writes to `src` must be
 // followed by fence_proxy_async_smem() and a barrier before the store is issued.

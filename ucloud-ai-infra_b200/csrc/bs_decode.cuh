@@ -161,6 +161,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) grid_dep_launch();
 
   const int M = p.M, KB = p.KB;
   const int nblk = p.N / 128;
@@ -187,6 +188,11 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
+      // The first stages' weights go to L2 while an earlier kernel may still be running.
+      for (int u = u0, t = t0, kb = kb0; u < u1 && u < u0 + S; ++u, kb = kb + 1 == KB ? 0 : kb + 1, t += kb == 0)
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) prefetch_weight_box(&tmW, w == 0 ? t : t + I_blk, kb, KB, p.b_tiled);
+      grid_dep_wait();
       BS_TR_DECL(1);
       for (int u = u0, t = t0, kb = kb0; u < u1; ++u, kb = kb + 1 == KB ? 0 : kb + 1, t += kb == 0) {
         BS_TR_MARK();
@@ -261,6 +267,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
     // operands of unit u+2 are loaded into the registers unit u has just used, from always-valid
     // addresses (the range's last unit, row 0 for padding tokens), so no store ever waits on a
     // load issued less than two units earlier.
+    grid_dep_wait();
     constexpr int TPL = (NTP + 32 * Cfg::kScaleWarps - 1) / (32 * Cfg::kScaleWarps);
     const int tok_base = (warp - scale_warp) * 32 * TPL + lane;
     struct Ops {
@@ -321,6 +328,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
   }
   } else {
     if constexpr (Cfg::kSplitRegs) regs_increase<Cfg::Regs::kConsumer>();
+    grid_dep_wait();
     // ------------------------------------------------------------ promotion + epilogue
     // Every promotion thread runs the same sequence of named barriers whether or not the CTA
     // aborted; after an abort only the waits, TMEM reads and stores are skipped.

@@ -82,6 +82,13 @@ __device__ __forceinline__ void load_weight_box(void* dst, const CUtensorMap* ma
     tma_load_2d(dst, map, bar, kb * 128, nb * 128, policy);
 }
 
+__device__ __forceinline__ void prefetch_weight_box(const CUtensorMap* map, int nb, int kb, int KB, int tiled) {
+  if (tiled)
+    tma_prefetch_l2_2d(map, 0, (nb * KB + kb) * 128);
+  else
+    tma_prefetch_l2_2d(map, kb * 128, nb * 128);
+}
+
 template <bool FUSED>
 __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -124,6 +131,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) grid_dep_launch();
 
   const int M = p.M, KB = p.KB;
   const int nblk = p.N / 128;                       // 128-row weight blocks
@@ -141,6 +149,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      grid_dep_wait();  // A and the output may belong to the previous kernel on the stream
       const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = policy_evict_normal();
       int s = 0;
@@ -228,6 +237,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
   }
   } else {
     regs_increase<Cfg::Regs::kConsumer>();
+    grid_dep_wait();
     // ------------------------------------------------------------ promotion + epilogue
     const int wg = warp >> 2;         // 0: columns 0-127 of the tile, 1: columns 128-255
     const int q = warp & 3;           // TMEM lane quarter

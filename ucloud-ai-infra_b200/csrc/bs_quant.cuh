@@ -18,6 +18,8 @@ constexpr int kQuantThreads = 256;
 __global__ void __launch_bounds__(kQuantThreads)
     k_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, uint8_t* __restrict__ A, float* __restrict__ As,
                   int M, int K) {
+  if (threadIdx.x == 0) grid_dep_launch();
+  grid_dep_wait();  // x may be the previous kernel's output
   const int KB = K / 128;
   const long long groups = static_cast<long long>(M) * KB;
   const int sub = threadIdx.x & 15;
