@@ -142,11 +142,11 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&pfull[i], 1);
-      mbar_init(&pempty[i], NPW);
+      mbar_init(&pempty[i], NPROMO);
     }
     for (int i = 0; i < NS; ++i) {
       mbar_init(&sfull[i], 32 * Cfg::kScaleWarps);
-      mbar_init(&sempty[i], NPW);
+      mbar_init(&sempty[i], NPROMO);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -365,9 +365,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
 #pragma unroll
           for (int w = 0; w < NWG; ++w) tmem_ld_run<TR>(tb + w * NTP, v + w * TR);
           tmem_ld_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pempty[b]);
+          mbar_arrive(&pempty[b]);  // this thread's columns are in registers
 #pragma unroll
           for (int w = 0; w < NWG; ++w)
 #pragma unroll
@@ -390,11 +388,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
               else
                 tmem_ld_run<kLast>(tb + w * NTP + c0, v);
               tmem_ld_wait();
-              if (w == NWG - 1 && c0 + CH >= TR) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&pempty[b]);
-              }
+              if (w == NWG - 1 && c0 + CH >= TR) mbar_arrive(&pempty[b]);
 #pragma unroll
               for (int i = 0; i < CH; i += 4) {
                 if (c0 + i < TR) {
@@ -406,8 +400,7 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sempty[slot]);
+        mbar_arrive(&sempty[slot]);  // this thread's reads of the slot are done
       }
       BS_TR_ADD(2);
       if (++b == NB) {

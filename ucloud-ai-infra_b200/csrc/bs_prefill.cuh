@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&pfull[i], 1);
-      mbar_init(&pempty[i], 8);
+      mbar_init(&pempty[i], 256);  // every promotion thread
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -289,9 +289,8 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
           for (int i = 0; i < 32; ++i) ffma2(acc[i], v[2 * i], v[2 * i + 1], sc2);
           tmem_ld64(tbase + 64, v);
           tmem_ld_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pempty[b]);
+          // every column of the buffer this thread needs is in registers (the loads completed)
+          mbar_arrive(&pempty[b]);
 #pragma unroll
           for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
         }
