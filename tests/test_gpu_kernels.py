@@ -77,7 +77,9 @@ GEMM_CASES = [
     (129, 512, 1024),
     (200, 384, 640),      # odd number of 128-column blocks: half-empty last tile
     (257, 2048, 5120),
-    (1024, 1024, 2048),
+    (1024, 1024, 2048),   # 256-row tiles on CTA pairs from here on
+    (600, 384, 640),      # last pair tile: peer rows all past M, half-empty last column tile
+    (520, 2048, 1024),    # last pair tile: 8 valid rows
 ]
 
 
@@ -106,7 +108,7 @@ def test_gemm_fp32_out_matches_oracle_tightly(cuda_lib, M, N, K):
     assert O.max_rel_error(C.cpu(), ref) <= 1e-3
 
 
-@pytest.mark.parametrize("M", [2, 64, 500])
+@pytest.mark.parametrize("M", [2, 64, 500, 1000])
 def test_gemm_deterministic_and_linear(cuda_lib, M):
     """Two launches give identical bytes; doubling As (exact in fp32) doubles C exactly."""
     A, B, As, Bs, _ = O.make_gemm_case(M, 1024, 2048, seed=M)
@@ -134,7 +136,7 @@ def _check_fused(Q, Qs, A, B, As, Bs):
 
 
 FUSED_CASES = [(1, 512, 1024), (8, 2048, 5120), (14, 1024, 5120), (56, 512, 2048), (112, 2048, 5120),
-               (128, 256, 512), (129, 512, 1024), (300, 1024, 5120), (1024, 512, 1024)]
+               (128, 256, 512), (129, 512, 1024), (300, 1024, 5120), (1024, 512, 1024), (600, 512, 1024)]
 
 
 @pytest.mark.parametrize("tiled", [True, False])

@@ -3,6 +3,7 @@
 #include <mutex>
 #include <utility>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include <cudaTypedefs.h>
@@ -101,6 +102,22 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int ntp_for(int M) { return ((M + 15) / 16) * 16; }
 
+// Prefill row count from which 256-row tiles on CTA pairs (cta_group::2) are used. Off unless the
+// environment sets BS_FP8_PAIR_MIN_ROWS (read once per process): the pair kernel is exact but measured
+// slower than one CTA per tile, because each K block's promotion handoff then crosses the pair.
+int pair_min_rows() {
+  static std::once_flag once;
+  static int rows = 0x7fffffff;
+  std::call_once(once, [] {
+    const char* v = std::getenv("BS_FP8_PAIR_MIN_ROWS");
+    if (v && *v) {
+      const long r = std::strtol(v, nullptr, 10);
+      if (r > 0 && r < 0x7fffffff) rows = static_cast<int>(r);
+    }
+  });
+  return rows;
+}
+
 // Grid of the decode kernels. When the weight tiles nearly match the SM count (>= 90%), one CTA
 // per tile streams whole tiles and no tile is split (no partial sums, no finishing CTA);
 // otherwise the stream-K split over one CTA per SM keeps every SM streaming equal bytes. Never
@@ -150,22 +167,32 @@ int prepare_kernel(int smem_bytes, int launch_regs) {
 // kernel on the stream is still running, and its threads wait (griddepcontrol.wait) before any
 // global access that could depend on that kernel.
 template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kern)(KArgs...), int grid, int block, int smem, cudaStream_t s, const char* where,
-               Args&&... args) {
+int launch_pdl_cluster(void (*kern)(KArgs...), int grid, int block, int smem, int cluster, cudaStream_t s,
+                       const char* where, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(static_cast<unsigned>(block));
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
   cudaGetLastError();  // clear an older error so the check below sees this launch only
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   if (e != cudaSuccess) return cuda_fail(e, where);
   return launch_status(where);
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), int grid, int block, int smem, cudaStream_t s, const char* where,
+               Args&&... args) {
+  return launch_pdl_cluster(kern, grid, block, smem, 1, s, where, std::forward<Args>(args)...);
 }
 
 template <bool FUSED, int NTP>
@@ -194,13 +221,52 @@ int dispatch_decode(int ntp, const CUtensorMap& tmW, const CUtensorMap& tmX, con
   }
 }
 
-template <bool FUSED>
+// Clusters of two of `kern` that fit on the device at once (0 if the query fails).
+template <auto kernel>
+int max_pair_clusters(int threads, int smem) {
+  struct State {
+    std::once_flag once[kMaxDevices];
+    int n[kMaxDevices];
+  };
+  static State st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  std::call_once(st.once[dev], [&] {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) n = 0;
+    cudaGetLastError();
+    st.n[dev] = n;
+  });
+  return st.n[dev];
+}
+
+// Persistent prefill launch. PAIR: clusters of two CTAs on one TPC compute 256-row tiles with
+// cta_group::2 MMAs, one cluster per co-resident SM pair.
+template <bool FUSED, bool PAIR>
 int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::GemmParams& p, int num_tiles,
                    int num_sms, cudaStream_t s) {
-  using Cfg = bs::PrefillCfg<FUSED>;
-  constexpr auto kern = bs::k_prefill<FUSED>;
+  using Cfg = bs::PrefillCfg<FUSED, PAIR>;
+  constexpr auto kern = bs::k_prefill<FUSED, PAIR>;
   const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::Regs::kLaunch);
   if (rc != BS_OK) return rc;
+  if constexpr (PAIR) {
+    int pairs = max_pair_clusters<kern>(Cfg::kThreads, Cfg::kSmemBytes);
+    if (pairs <= 0) pairs = num_sms / 2;
+    if (pairs > num_tiles) pairs = num_tiles;
+    return launch_pdl_cluster(kern, 2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, 2, s, "k_prefill<pair> launch", tmA,
+                              tmB, p);
+  }
   const int grid = num_tiles < num_sms ? num_tiles : num_sms;
   return launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, s, "k_prefill launch", tmA, tmB, p);
 }
@@ -228,12 +294,7 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   p.ldc = fused ? N / 2 : ldc;
   p.b_tiled = b_tiled;
   p.out_f32 = fused ? 0 : out_dtype;
-  // Prefill raster: all M tiles in one group when that A panel stays in L2 (each weight tile is
-  // then read from HBM once), else 16 M tiles per group.
-  {
-    const long long a_panel = static_cast<long long>(M) * K;
-    p.group_m = a_panel <= (48ll << 20) ? (M + 127) / 128 : 16;
-  }
+
   p.As = As;
   p.Bs = Bs;
   p.out = out;
@@ -266,10 +327,19 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
 
   CUtensorMap tmA;
   if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
-  const int num_m = (M + 127) / 128;
   const int num_n = fused ? N / 256 : (N / 128 + 1) / 2;
-  return fused ? launch_prefill<true>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
-               : launch_prefill<false>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
+  // 256-row tiles on CTA pairs once there are enough rows for them
+  const bool pair = M >= pair_min_rows();
+  const int rows = pair ? 256 : 128;
+  const int num_m = (M + rows - 1) / rows;
+  // Raster: one group over every M tile when the whole A panel stays in L2 (each weight tile is then
+  // read from HBM once), else groups of 2048 rows.
+  p.group_m = static_cast<long long>(M) * K <= (48ll << 20) ? num_m : 2048 / rows;
+  if (pair)
+    return fused ? launch_prefill<true, true>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
+                 : launch_prefill<false, true>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
+  return fused ? launch_prefill<true, false>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
+               : launch_prefill<false, false>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
 }
 
 // ------------------------------------------------------------ allocation-free GEMM entry point

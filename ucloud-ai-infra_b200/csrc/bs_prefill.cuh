@@ -47,18 +47,19 @@ struct GemmParams {
   int* status;       // library status word
 };
 
-template <bool FUSED>
+template <bool FUSED, bool PAIR = false>
 struct PrefillCfg {
   using Regs = RegSplit<384, 168, 40, 232>;
   static constexpr int kThreads = Regs::kThreads;
-  static constexpr int kStages = FUSED ? 3 : 4;
+  static constexpr int kStages = PAIR ? (FUSED ? 4 : 6) : (FUSED ? 3 : 4);
   static constexpr int kABytes = 128 * 128;
-  static constexpr int kBBytes = 256 * 128;
+  static constexpr int kBBytes = (PAIR ? 128 : 256) * 128;  // a pair CTA holds half of the weight rows
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 + 128 * 2 * 4 : 0;  // half groups + amax halves
   static constexpr int kBarOff = kStages * kStageBytes + kXchBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers, then slack for 1 KB alignment
   static constexpr int kTmemCols = 512;
+  static constexpr int kRows = PAIR ? 256 : 128;  // output rows per tile
 };
 
 // Tile index -> (m tile, n tile), grouped so that CTAs running together share A and B tiles in L2.
@@ -89,11 +90,11 @@ __device__ __forceinline__ void prefetch_weight_box(const CUtensorMap* map, int 
     tma_prefetch_l2_2d(map, kb * 128, nb * 128);
 }
 
-template <bool FUSED>
-__global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
+template <bool FUSED, bool PAIR>
+__global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const GemmParams p) {
-  using Cfg = PrefillCfg<FUSED>;
+  using Cfg = PrefillCfg<FUSED, PAIR>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -109,26 +110,35 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Pair: rank 0 (leader) issues the MMAs for both CTAs; rank 1 forwards "stage landed" to it and
+  // releases TMEM buffers on its barriers.
+  const uint32_t cr = PAIR ? cluster_ctarank() : 0u;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], (PAIR && cr == 0) ? 2 : 1);  // leader: own producer + peer's forwarder
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&pfull[i], 1);
-      mbar_init(&pempty[i], 256);  // every promotion thread
+      mbar_init(&pempty[i], PAIR ? 256 + 8 : 256);  // own promotion threads (+ the peer's 8 warps)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 9) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // the peer's barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) grid_dep_launch();
@@ -136,9 +146,12 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
   const int M = p.M, KB = p.KB;
   const int nblk = p.N / 128;                       // 128-row weight blocks
   const int I_blk = FUSED ? nblk / 2 : 0;           // fused: gate blocks (= up blocks)
-  const int num_m = (M + 127) / 128;
+  const int num_m = (M + Cfg::kRows - 1) / Cfg::kRows;
   const int num_n = FUSED ? I_blk : (nblk + 1) / 2;
   const int num_tiles = num_m * num_n;
+  const int tile0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tstep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int row0 = PAIR ? static_cast<int>(cr) * 128 : 0;  // this CTA's first row inside a tile
 
   // Each role changes its register budget at the top of its own branch: code after a merge of
   // the two branches must fit the smaller budget, and only the short teardown follows one.
@@ -156,7 +169,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
       BS_TR_DECL(1);
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
         int tm, tn;
         prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
         const int nb0 = FUSED ? tn : 2 * tn;
@@ -170,9 +183,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
           BS_TR_ADD(0);
           uint8_t* st = smem + s * Cfg::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          tma_load_2d(st, &tmA, &full[s], kb * 128, tm * 128, pol_a);
-          load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
-          load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
+          tma_load_2d(st, &tmA, &full[s], kb * 128, tm * Cfg::kRows + row0, pol_a);
+          if constexpr (PAIR) {
+            load_weight_box(st + Cfg::kABytes, &tmB, &full[s], cr == 0 ? nb0 : nb1, kb, KB, p.b_tiled, pol_b);
+          } else {
+            load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
+            load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
+          }
           issued |= 1u << s;
           parity_bits = (parity_bits & ~(1u << s)) | (ph << s);
           if (++s == S) {
@@ -191,13 +208,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+    if (lane == 0 && cr == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(Cfg::kRows, 256);
       int s = 0, b = 0;
       uint32_t ph = 0, pph = 0;
       bool ok = true;
       BS_TR_DECL(2);
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
         for (int kb = 0; kb < KB; ++kb) {
           BS_TR_MARK();
           if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) {
@@ -214,11 +231,20 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
           const uint32_t a0 = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t b0 = a0 + Cfg::kABytes;
           const uint32_t d = tmem + static_cast<uint32_t>(b * 256);
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_e4m3(d, desc_kmajor_sw128(a0 + 32 * k), desc_kmajor_sw128(b0 + 32 * k), idesc, k > 0 ? 1u : 0u);
-          mma_commit(&empty[s]);
-          mma_commit(&pfull[b]);
+            for (int k = 0; k < 4; ++k)
+              mma_e4m3_pair(d, desc_kmajor_sw128(a0 + 32 * k), desc_kmajor_sw128(b0 + 32 * k), idesc,
+                            k > 0 ? 1u : 0u);
+            mma_commit_pair(&empty[s], 3);  // both CTAs' stage s is free again
+            mma_commit_pair(&pfull[b], 3);  // both CTAs' partial buffer b is ready
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_e4m3(d, desc_kmajor_sw128(a0 + 32 * k), desc_kmajor_sw128(b0 + 32 * k), idesc, k > 0 ? 1u : 0u);
+            mma_commit(&empty[s]);
+            mma_commit(&pfull[b]);
+          }
           if (++s == S) {
             s = 0;
             ph ^= 1;
@@ -231,8 +257,34 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
       }
       BS_TR_FLUSH(4, 2);
       // Every MMA issued so far completes before TMEM is released.
-      mma_commit(drain);
+      if constexpr (PAIR)
+        mma_commit_pair(drain, 1);
+      else
+        mma_commit(drain);
       mbar_wait(drain, 0, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
+    }
+  } else if (PAIR && warp == 10 && cr == 1) {
+    // ------------------------------------------------------------ stage forwarder (pair peer)
+    // The peer's TMA loads complete on its own full barrier (so an aborting CTA can drain its own
+    // copies); this warp passes each completed stage on to the leader's full barrier.
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = tile0; tile < num_tiles; tile += tstep) {
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_remote(mapa_shared(&full[s], 0));
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
     }
   }
   } else {
@@ -249,10 +301,10 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
     uint32_t pph = 0;
     bool ok = true;
     BS_TR_DECL(4);
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int tm, tn;
       prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
-      const int row = tm * 128 + r;
+      const int row = tm * Cfg::kRows + row0 + r;
       const bool row_ok = row < M;
       const int nb = FUSED ? (wg == 0 ? tn : tn + I_blk) : 2 * tn + wg;
       const bool col_ok = nb < nblk;
@@ -290,7 +342,15 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
           tmem_ld64(tbase + 64, v);
           tmem_ld_wait();
           // every column of the buffer this thread needs is in registers (the loads completed)
-          mbar_arrive(&pempty[b]);
+          if (!PAIR || cr == 0) {
+            mbar_arrive(&pempty[b]);
+          } else {
+            // The leader's MMA reuses it: one arrival per warp on the leader's barrier, sent with a pair
+            // commit (no MMA of this thread is pending, so it arrives at once); measured much faster
+            // than a cluster-scope release arrive.
+            __syncwarp();
+            if (lane == 0) mma_commit_pair_to(mapa_shared(&pempty[b], 0));
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
         }
@@ -397,10 +457,16 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED>::kThreads, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  // Pair: neither CTA leaves while the leader's MMAs (drained above) or the peer's remote
+  // arrivals may still touch the other's shared memory or TMEM.
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 9) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+    else
+      tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 }
 
