@@ -6,8 +6,9 @@ One step = one MLP of BASELINE config 3 at M = 8192 tokens: activation group qua
 fused gate_up (K=5120, N2=2x17408) + SiLU*up + per-token-group quant -> down_proj
 (K=17408, N=5120) -> bf16 [8192, 5120], through the drop-in API (GatedMLP with relayouted
 weights; the SGLang call sites are stood in by fp8_hand_b200.sglang_compat). With N > 1 the same
-MLP runs tensor-parallel (config 5): gate_up column-parallel, down_proj row-parallel, one NCCL
-all_reduce of fp32 partials; total work is fixed, so scaling is "strong".
+MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel into
+bf16 partials summed by one NCCL all_reduce (optionally in row chunks overlapped with compute,
+--tp-chunks); total work is fixed, so scaling is "strong".
 
 Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e`
 repeats the step with the input copied from pinned host memory and the output copied back inside
@@ -42,6 +43,11 @@ M_PREFILL = 8192
 HIDDEN = 5120
 INTER = 17408
 DECODE_MS = (1, 8, 14, 56, 112)
+# Tensor parallel (N > 1): rows per MLP step split into TP_CHUNKS chunks whose all_reduce overlaps the next
+# chunk's GEMMs; the GEMM kernels' persistent grids use TP_SM_LIMIT SMs, NCCL at most TP_NCCL_CTAS CTAs.
+TP_CHUNKS = 1
+TP_NCCL_CTAS = 16
+TP_SM_LIMIT = 148 - TP_NCCL_CTAS
 # RTX 4090 hand kernels: fused gate_up 9.25 ms + down_proj 4.595 ms at M = 8192.
 REF_4090_MLP_MS = 9.25 + 4.595
 FP8_NOMINAL_TFLOPS = 4500.0
@@ -179,7 +185,7 @@ def fp8_peak_tflops(device) -> float:
 
 
 # ----------------------------------------------------------------------------- our arm
-def build_mlp(rank, world, device):
+def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS):
     from fp8_hand_b200 import fp8_hand_sm100, sglang_compat, tp
     gu_q, gu_s, dn_q, dn_s = make_weights(device)
     if world == 1:
@@ -190,14 +196,15 @@ def build_mlp(rank, world, device):
         return (mlp, (mlp.gate_up_proj.weight.tiles, gu_s), (mlp.down_proj.weight.tiles, dn_s), 2 * INTER)
     shard = tp.make_shard(gu_q, gu_s, dn_q, dn_s, rank, world, device=device, tiled=True)
     del gu_q, dn_q
-    return (tp.TensorParallelMLP(shard), (shard.gate_up, shard.gate_up_scale), (shard.down, shard.down_scale),
+    return (tp.TensorParallelMLP(shard, chunks=tp_chunks), (shard.gate_up, shard.gate_up_scale),
+            (shard.down, shard.down_scale),
             2 * INTER // world)
 
 
 def run_ours(args, rank, world, device) -> dict | None:
     from fp8_hand_b200 import ops
     torch.cuda.set_device(device)
-    mlp, (gu_tiles, gu_s), (dn_tiles, dn_s), n2_local = build_mlp(rank, world, device)
+    mlp, (gu_tiles, gu_s), (dn_tiles, dn_s), n2_local = build_mlp(rank, world, device, args.tp_chunks)
     x = make_x(M_PREFILL, device)
     stream = torch.cuda.current_stream(device)
 
@@ -356,7 +363,10 @@ def run_ours(args, rank, world, device) -> dict | None:
         "config": {
             "workload": "config[2] MLP at M=8192: group quant -> fused gate_up+SiLU*up+quant (K=5120, N2=34816) "
                         "-> down_proj (K=17408, N=5120), bf16 in/out" +
-                        (f"; config[4] tensor-parallel tp={world}, fp32 partials + NCCL all_reduce" if world > 1 else ""),
+                        (f"; config[4] tensor-parallel tp={world}, bf16 partials + NCCL all_reduce"
+                         + (f" in {args.tp_chunks} row chunks overlapped with compute, GEMM grids on "
+                            f"{os.environ.get('BS_FP8_SM_LIMIT', 'all')} SMs" if args.tp_chunks > 1 else "")
+                         if world > 1 else ""),
             "M": M_PREFILL, "hidden": HIDDEN, "intermediate": INTER, "parallelism": f"tp{world}",
             "l2": "inputs larger than L2 (weights 267 MB + x 84 MB per step vs 126 MB L2)",
         },
@@ -460,6 +470,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-rows", type=int, default=8192)
+    ap.add_argument("--tp-chunks", type=int, default=TP_CHUNKS,
+                    help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
     ap.add_argument("--ref-rows", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
@@ -476,7 +488,10 @@ def main() -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1:
+    if world > 1 and args.tp_chunks > 1:
+        # overlap needs free SMs: read by the library and by NCCL when they first initialise
+        os.environ.setdefault("BS_FP8_SM_LIMIT", str(TP_SM_LIMIT))
+        os.environ.setdefault("NCCL_MAX_CTAS", str(TP_NCCL_CTAS))
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     try:

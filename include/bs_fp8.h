@@ -103,7 +103,8 @@ int bs_fp8_status(int* code, int clear);
  * path without any fault. No reference counterpart (the reference has no bounded waits). */
 int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
-/* Number of SMs the kernels size their persistent grids for (current device). */
+/* Number of SMs the kernels size their persistent grids for (current device): all of them, or
+ * BS_FP8_SM_LIMIT from the environment when that is smaller (SMs left to concurrent kernels). */
 int bs_fp8_num_sms(void);
 
 /* Human-readable text for a status code. */

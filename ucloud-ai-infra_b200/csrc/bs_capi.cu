@@ -67,6 +67,12 @@ DeviceState* device_state() {
   std::call_once(d->once, [d, dev] {
     cudaError_t e = cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) d->err = cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+    // BS_FP8_SM_LIMIT caps the CTAs of the persistent GEMM kernels, leaving the other SMs to kernels
+    // that run at the same time (e.g. the collectives of a tensor-parallel layer).
+    if (const char* v = std::getenv("BS_FP8_SM_LIMIT")) {
+      const long lim = std::strtol(v, nullptr, 10);
+      if (lim >= 8 && lim < d->num_sms) d->num_sms = static_cast<int>(lim);
+    }
     void* sym = nullptr;
     e = cudaGetSymbolAddress(&sym, g_bs_status);
     if (e != cudaSuccess) d->err = cuda_fail(e, "cudaGetSymbolAddress(status word)");

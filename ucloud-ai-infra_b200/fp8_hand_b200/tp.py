@@ -11,8 +11,10 @@ B200-side extension the north star asks for:
            and the matching scale columns. The fused kernel's quant groups (128 wide) line up
            with those columns, so each rank's (Q_r, Qs_r) is exactly its slice of the 1-GPU
            (Q, Qs).
-  reduce   one all_reduce(sum) of the [M, H] partials per MLP, fp32 by default (bf16 optional),
-           on the compute stream.
+  reduce   all_reduce(sum) of the bf16 [M, H] partials (fp32 optional). With chunks > 1 the rows are
+           processed in chunks and each chunk's all_reduce runs asynchronously while the next chunk
+           computes; the library's persistent kernels then leave SMs free for NCCL when
+           BS_FP8_SM_LIMIT caps their grid.
 
 The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
 the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
@@ -79,13 +81,15 @@ def make_shard(gate_up, gate_up_scale, down, down_scale, rank: int, world: int, 
 class TensorParallelMLP:
     """x [M, H] bf16 (replicated) -> quant -> fused gate_up_r -> down_r -> all_reduce -> [M, H]."""
 
-    def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.float32, compute=None):
+    def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.bfloat16, compute=None,
+                 chunks: int = 1):
         if compute is None:
             from . import ops as compute
         self.shard = shard
         self.group = group
         self.partial_dtype = partial_dtype
         self.compute = compute
+        self.chunks = max(1, int(chunks))
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
 
     def partial(self, x: torch.Tensor) -> torch.Tensor:
@@ -95,8 +99,28 @@ class TensorParallelMLP:
         Q, Qs = c.gemm_silu_quant(A, s.gate_up, As, s.gate_up_scale, b_tiled=s.tiled)
         return c.gemm(Q, s.down, Qs, s.down_scale, b_tiled=s.tiled, out_dtype=self.partial_dtype)
 
+    def _chunk_rows(self, m: int) -> list[tuple[int, int]]:
+        step = -(-m // self.chunks)
+        step = -(-step // BLOCK) * BLOCK  # whole 128-row tiles per chunk
+        return [(r, min(r + step, m)) for r in range(0, m, step)]
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        part = self.partial(x)
-        if self.world > 1:
-            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
-        return part.to(torch.bfloat16)
+        if self.world == 1 or self.chunks == 1 or x.shape[0] <= BLOCK:
+            part = self.partial(x)
+            if self.world > 1:
+                dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+            return part.to(torch.bfloat16)
+        # Chunked rows: chunk i's all_reduce overlaps chunk i+1's GEMMs. Every rank issues the same
+        # collectives in the same order.
+        c, s = self.compute, self.shard
+        A, As = c.group_quant(x)
+        out = torch.empty((x.shape[0], s.down.shape[0] * (BLOCK if s.tiled else 1)), dtype=self.partial_dtype,
+                          device=x.device)
+        works = []
+        for r0, r1 in self._chunk_rows(x.shape[0]):
+            Q, Qs = c.gemm_silu_quant(A[r0:r1], s.gate_up, As[r0:r1], s.gate_up_scale, b_tiled=s.tiled)
+            c.gemm(Q, s.down, Qs, s.down_scale, b_tiled=s.tiled, out=out[r0:r1])
+            works.append(dist.all_reduce(out[r0:r1], op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+        for w in works:
+            w.wait()
+        return out.to(torch.bfloat16)
