@@ -164,6 +164,42 @@ def max_over_ranks(v: float, world: int, device) -> float:
     return t.item()
 
 
+def linear_set(device, hbm, graph_us) -> dict:
+    """the other block-FP8 linears of a layer at M=8192 (TFLOP/s, event-timed median of
+    5 launches) and the vocab-sized lm_head at decode sizes (GB/s, CUDA graph), random-init weights."""
+    from fp8_hand_b200 import kernel_bench as kbench, ops
+    out = {}
+    for name, n, k in (("qkv", 10240, 5120), ("o", 5120, 6144)):
+        tiles, s = kbench._weights(n, k, device)
+        A, As = kbench._acts(M_PREFILL, k, device)
+        C = torch.empty(M_PREFILL, n, dtype=torch.bfloat16, device=device)
+        for _ in range(3):
+            ops.gemm(A, tiles, As, s, b_tiled=True, out=C)
+        times = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ops.gemm(A, tiles, As, s, b_tiled=True, out=C)
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        out[f"{name}_m{M_PREFILL}_k{k}_n{n}"] = {"ms": round(ms, 4),
+                                                 "TFLOP/s": round(2.0 * M_PREFILL * n * k / (ms * 1e-3) / 1e12, 1)}
+        del tiles, s, A, As, C
+    n, k = 248320, 5120
+    tiles, s = kbench._weights(n, k, device)
+    for m in (1, 112):
+        A, As = kbench._acts(m, k, device)
+        C = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+        us = graph_us(lambda: ops.gemm(A, tiles, As, s, b_tiled=True, out=C))
+        gbs = (n * k + m * k * (1 + 4 / 128) + 4 * (n // 128) * (k // 128) + 2 * m * n) / (us * 1e-6) / 1e9
+        out[f"lm_head_m{m}_k{k}_n{n}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+    del tiles, s
+    torch.cuda.empty_cache()
+    return out
+
+
 def fp8_peak_tflops(device) -> float:
     """Dense e4m3 tensor peak measured as a cuBLASLt burst (torch._scaled_mm, 8192^3)."""
     n = 8192
@@ -337,6 +373,7 @@ def run_ours(args, rank, world, device) -> dict | None:
         decode_down[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
 
     fp8_peak = fp8_peak_tflops(device) if rank == 0 else None
+    linears = linear_set(device, hbm, graph_us) if world == 1 else None
     if rank != 0:
         return None
     fused_tflops = 2.0 * M_PREFILL * n2_local * HIDDEN / (fused_ms * 1e-3) / 1e12
@@ -388,6 +425,7 @@ def run_ours(args, rank, world, device) -> dict | None:
                 "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                 "d2h_bytes_per_step": oh.numel() * oh.element_size()},
         "gpu_launches": 3 * args.steps,
+        **({"linear_set": linears} if linears else {}),
         "clocks": clk.summary(),
     }
     if world == 1:

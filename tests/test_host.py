@@ -68,9 +68,14 @@ def test_argument_validation_needs_no_gpu(lib):
 
 
 def _decode_grid(sms, tiles, kb):
-    """One CTA per tile when tiles nearly match the SMs (>= 90%), else one CTA per SM (stream-K)."""
+    """One CTA per tile when tiles nearly match the SMs (>= 90%); s equal K splits per tile when that fills
+    >= 95% of the SMs; else one CTA per SM (stream-K)."""
     if tiles <= sms and 10 * tiles >= 9 * sms:
         return tiles
+    if tiles < sms:
+        s = sms // tiles
+        if 2 <= s <= kb and 20 * tiles * s >= 19 * sms:
+            return tiles * s
     return min(sms, tiles * kb)
 
 

@@ -125,11 +125,17 @@ int pair_min_rows() {
 }
 
 // Grid of the decode kernels. When the weight tiles nearly match the SM count (>= 90%), one CTA
-// per tile streams whole tiles and no tile is split (no partial sums, no finishing CTA);
-// otherwise the stream-K split over one CTA per SM keeps every SM streaming equal bytes. Never
+// per tile streams whole tiles and no tile is split (no partial sums, no finishing CTA). When a
+// whole number s of CTAs per tile still fills >= 95% of the SMs, each tile is split into s equal
+// K ranges (every CTA holds one segment of one tile: one fix-up, none at a tile boundary).
+// Otherwise the stream-K split over one CTA per SM keeps every SM streaming equal bytes. Never
 // more CTAs than (tile, K block) units.
 int decode_grid(int num_sms, int tiles, int KB) {
   if (tiles <= num_sms && 10 * tiles >= 9 * num_sms) return tiles;
+  if (tiles < num_sms) {
+    const int s = num_sms / tiles;
+    if (s >= 2 && s <= KB && 20 * tiles * s >= 19 * num_sms) return tiles * s;
+  }
   const long long units = static_cast<long long>(tiles) * KB;
   return static_cast<int>(units < num_sms ? units : num_sms);
 }
