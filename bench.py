@@ -526,10 +526,11 @@ def main() -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1 and args.tp_chunks > 1:
-        # overlap needs free SMs: read by the library and by NCCL when they first initialise
-        os.environ.setdefault("BS_FP8_SM_LIMIT", str(TP_SM_LIMIT))
-        os.environ.setdefault("NCCL_MAX_CTAS", str(TP_NCCL_CTAS))
+    if world > 1:
+        if args.tp_chunks > 1:
+            # overlap needs free SMs: read by the library and by NCCL when they first initialise
+            os.environ.setdefault("BS_FP8_SM_LIMIT", str(TP_SM_LIMIT))
+            os.environ.setdefault("NCCL_MAX_CTAS", str(TP_NCCL_CTAS))
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     try:
