@@ -166,7 +166,8 @@ def max_over_ranks(v: float, world: int, device) -> float:
 
 def linear_set(device, hbm, graph_us) -> dict:
     """the other block-FP8 linears of a layer at M=8192 (TFLOP/s, event-timed median of
-    5 launches) and the vocab-sized lm_head at decode sizes (GB/s, CUDA graph), random-init weights."""
+    5 launches), the fused RMSNorm + activation quant, and the vocab-sized lm_head at decode sizes (GB/s,
+    CUDA graph), random-init weights."""
     from fp8_hand_b200 import kernel_bench as kbench, ops
     out = {}
     for name, n, k in (("qkv", 10240, 5120), ("o", 5120, 6144)):
@@ -187,6 +188,16 @@ def linear_set(device, hbm, graph_us) -> dict:
         out[f"{name}_m{M_PREFILL}_k{k}_n{n}"] = {"ms": round(ms, 4),
                                                  "TFLOP/s": round(2.0 * M_PREFILL * n * k / (ms * 1e-3) / 1e12, 1)}
         del tiles, s, A, As, C
+    # RMSNorm fused with the activation quant, with and without the fused residual add
+    k = HIDDEN
+    w = torch.ones(k, dtype=torch.bfloat16, device=device)
+    for m, add in ((M_PREFILL, False), (M_PREFILL, True), (112, True)):
+        xm = make_x(m, device, seed=4, outlier_frac=0.0)
+        res = make_x(m, device, seed=5, outlier_frac=0.0) if add else None
+        us = graph_us(lambda: ops.rmsnorm_group_quant(xm, w, 1e-6, residual=res))
+        nbytes = m * k * (2 + 1 + 4 / 128) + (4 * m * k if add else 0) + 2 * k
+        out[f"rmsnorm_quant_m{m}_k{k}" + ("_add" if add else "")] = {
+            "us": round(us, 2), "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1), "frac_hbm": round(nbytes / (us * 1e-6) / 1e9 / hbm, 3)}
     n, k = 248320, 5120
     tiles, s = kbench._weights(n, k, device)
     for m in (1, 112):

@@ -88,6 +88,16 @@ size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused);
  * arithmetic of the reference's torch quantiser (scripts/fp8_gemm_factor_check.py:22-27). */
 int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K, void* stream);
 
+/* RMSNorm fused with the per-token-group quant (the activation quant of the next linear), without
+ * storing the bf16 norm output: h = x, or h = bf16(x + residual) written back to residual (row stride
+ * ldr; residual may be NULL); y = bf16((h * (1 / sqrt(mean(h^2) + eps))) * weight[K]); then A, As as
+ * bs_fp8_group_quant(y). Replaces the pair "RMSNorm -> per_token_group_quant_fp8(., 128)" ahead of
+ * the hooked linears (H:690-693), in the way the reference fuses the group quant into its GDN output
+ * norm (patches/apply_sglang_gdn_prefill.py:538-591). Bit-exact with that pair computed with the
+ * fixed summation order stated in the kernel. K: multiple of 128, at most 16384. */
+int bs_fp8_rmsnorm_group_quant(const void* x, int ldx, void* residual, int ldr, const void* weight, float eps,
+                               void* A, float* As, int M, int K, void* stream);
+
 /* Tile-first weight pre-pack: tiles[nb][kb][r][c] = W[nb*128 + r][kb*128 + c] for e4m3 W [N, K].
  * Replaces the permute in `relayout(model)` (H:667). W and tiles must not overlap. */
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream);

@@ -14,6 +14,9 @@ It restates, in torch-CPU / numpy code, the reference's own CPU-runnable arithme
   silu_quant         the fused epilogue, H:532-579: y = silu(g) * u, scale = max(amax, 1e-10) / 448,
                      inv = 1 / scale, q = sat_e4m3(y * inv)
   relayout_tiles     the tile-first pre-pack, H:667
+  rmsnorm_group_quant  RMSNorm fused with the group quant, as the reference fuses it into its GDN output
+                     norm (patches/apply_sglang_gdn_prefill.py:538-591), with the bf16 rounding of the
+                     unfused norm output and the library kernel's summation order
   make_*             the seeded input generators of the north-star configs (weights N(0, 0.02)
                      quantised per 128x128 block, activations N(0, 1) quantised per 1x128 group,
                      optionally 1% of rows scaled x50), following scripts/fp8_gemm_factor_check.py:53-61
@@ -48,6 +51,43 @@ def quant_block(x: torch.Tensor, rows: int, cols: int) -> tuple[torch.Tensor, to
 def group_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Activation quant, 1 x 128 groups."""
     return quant_block(x, 1, BLOCK)
+
+
+def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
+    """RMSNorm then the per-token-group quant, with the rounding points of the unfused pair (the bf16 norm
+    output, then quant_block) and the library kernel's fixed fp32 summation order for sum(h^2), which
+    depends on K only: thread t of a 256-thread row adds the squares of its elements 8(t + 256j) + e in
+    (j, e) order; each 32-thread warp combines its threads in a butterfly (xor 16, 8, 4, 2, 1); then
+    ss = ((w0 + w1) + w2) + ... + w7. rs = 1 / sqrt(ss / K + eps) in IEEE fp32; y = bf16((h * rs) * w).
+    With residual: h = bf16(x + residual), which is also returned (the fused add writes it back).
+    Returns (A, As, h_bf16 or None)."""
+    xf = x.float()
+    h = (xf + residual.float()).to(torch.bfloat16).float() if residual is not None else xf
+    M, K = h.shape
+    nch = K // 8
+    hn = h.numpy().astype(np.float32)
+    sq = hn * hn  # fp32 products, rounded once
+    threads = np.zeros((M, 256), dtype=np.float32)
+    tid = np.arange(256)
+    for j in range((nch + 255) // 256):
+        c = 256 * j + tid
+        live = c < nch
+        for e in range(8):
+            cols = np.where(live, c * 8 + e, 0)
+            add = np.where(live[None, :], sq[:, cols], np.float32(0))
+            threads = np.where(live[None, :], threads + add, threads).astype(np.float32)
+    warps = threads.reshape(M, 8, 32)
+    lane = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        warps = (warps + warps[:, :, lane ^ o]).astype(np.float32)
+    ss = warps[:, 0, 0]
+    for i in range(1, 8):
+        ss = (ss + warps[:, i, 0]).astype(np.float32)
+    rs = np.float32(1) / np.sqrt((ss / np.float32(K) + np.float32(eps)).astype(np.float32))
+    rs_t = torch.from_numpy(rs.astype(np.float32))
+    y = ((h * rs_t[:, None]) * weight.float()[None, :]).to(torch.bfloat16)
+    A, As = quant_block(y.float(), 1, BLOCK)
+    return A, As, (h.to(torch.bfloat16) if residual is not None else None)
 
 
 def weight_quant(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -54,6 +54,34 @@ def test_group_quant_strided_rows(cuda_lib):
     assert torch.equal(A.cpu().view(torch.uint8), qr.view(torch.uint8)) and torch.equal(As.cpu(), sr)
 
 
+@pytest.mark.parametrize("M,K,fused_add", [(1, 128, False), (7, 640, True), (300, 5120, False), (33, 5120, True),
+                                            (64, 16384, True)])
+def test_rmsnorm_group_quant_bit_exact(cuda_lib, M, K, fused_add):
+    """Fused RMSNorm + group quant against the oracle restatement (same rounding points and summation
+    order): e4m3 bytes, scales and the updated residual all bit-exact."""
+    g = torch.Generator().manual_seed(M * 7 + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    x[0, :128] *= 40.0  # a group far above the row's rms
+    w = (1 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    r = torch.randn(M, K, generator=g).to(torch.bfloat16) if fused_add else None
+    A_ref, As_ref, h_ref = O.rmsnorm_group_quant(x, w, 1e-6, r)
+    rd = r.cuda() if fused_add else None
+    A, As = _ops().rmsnorm_group_quant(x.cuda(), w.cuda(), 1e-6, residual=rd)
+    torch.cuda.synchronize()
+    assert torch.equal(A.cpu().view(torch.uint8), A_ref.view(torch.uint8))
+    assert torch.equal(As.cpu(), As_ref)
+    if fused_add:
+        assert torch.equal(rd.cpu(), h_ref)
+
+
+def test_rmsnorm_group_quant_strided_rows(cuda_lib):
+    x = torch.randn(9, 384, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    w = torch.ones(256, dtype=torch.bfloat16)
+    A_ref, As_ref, _ = O.rmsnorm_group_quant(x[:, :256].contiguous(), w, 1e-5)
+    A, As = _ops().rmsnorm_group_quant(x.cuda()[:, :256], w.cuda(), 1e-5)
+    assert torch.equal(A.cpu().view(torch.uint8), A_ref.view(torch.uint8)) and torch.equal(As.cpu(), As_ref)
+
+
 @pytest.mark.parametrize("N,K", [(128, 128), (384, 640), (256, 5120)])
 def test_pack_tiles_bit_exact(cuda_lib, N, K):
     g = torch.Generator().manual_seed(N * 7 + K)

@@ -63,6 +63,11 @@ def test_argument_validation_needs_no_gpu(lib):
     assert lib.bs_fp8_group_quant(None, 256, None, None, 0, 256, s) == 0
     assert lib.bs_fp8_group_quant(None, 256, None, None, 4, 200, s) == 1
     assert lib.bs_fp8_pack_tiles(None, None, 100, 128, s) == 1
+    assert lib.bs_fp8_rmsnorm_group_quant(None, 256, None, 256, None, 1e-6, None, None, 0, 256, s) == 0
+    assert lib.bs_fp8_rmsnorm_group_quant(None, 256, None, 256, None, 1e-6, None, None, 4, 200, s) == 1
+    assert lib.bs_fp8_rmsnorm_group_quant(None, 256, None, 256, None, -1.0, None, None, 4, 256, s) == 1
+    assert lib.bs_fp8_rmsnorm_group_quant(None, 256, None, 256, None, 1e-6, None, None, 4, 256, s) == 1
+    assert lib.bs_fp8_rmsnorm_group_quant(None, 17408, None, 17408, None, 1e-6, None, None, 4, 17408, s) == 1
     # null pointers with a real shape
     assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
 

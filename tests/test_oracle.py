@@ -96,3 +96,23 @@ def test_e4m3_ulp_distance():
     b = torch.tensor([0.0, 1.125, -1.125, 416.0, -2.0]).to(torch.float8_e4m3fn)
     d = O.e4m3_ulp_distance(a, b).tolist()
     assert d[:4] == [0, 1, 1, 1] and d[4] > 1
+
+
+def test_rmsnorm_quant_oracle_matches_plain_torch():
+    """The fused norm+quant restatement (fixed summation order) against the plain torch formulation of the
+    unfused pair: RMSNorm in fp32 rounded to bf16, then the group quant. Only sum(h^2) is ordered
+    differently, so scales agree to fp32 rounding and codes differ by at most one e4m3 step, rarely."""
+    g = torch.Generator().manual_seed(5)
+    for M, K, fused_add in ((7, 640, False), (33, 5120, True)):
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+        r = torch.randn(M, K, generator=g).to(torch.bfloat16) if fused_add else None
+        A, As, h = O.rmsnorm_group_quant(x, w, 1e-6, r)
+        hh = (x.float() + r.float()).to(torch.bfloat16).float() if fused_add else x.float()
+        y = (hh * torch.rsqrt(hh.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(torch.bfloat16)
+        A2, As2 = O.group_quant(y)
+        assert torch.allclose(As, As2, rtol=1e-6, atol=0)
+        d = O.e4m3_ulp_distance(A, A2)
+        assert d.max().item() <= 1 and (d > 0).float().mean().item() <= 1e-3
+        if fused_add:
+            assert torch.equal(h, hh.to(torch.bfloat16))

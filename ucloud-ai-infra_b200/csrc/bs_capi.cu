@@ -464,6 +464,28 @@ int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K,
                     M, K);
 }
 
+int bs_fp8_rmsnorm_group_quant(const void* x, int ldx, void* residual, int ldr, const void* weight, float eps,
+                               void* A, float* As, int M, int K, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0 || ldx < K || ldx % 8 != 0) return BS_ERR_ARG;
+  if (residual && (ldr < K || ldr % 8 != 0)) return BS_ERR_ARG;
+  if (!(eps >= 0.f)) return BS_ERR_ARG;
+  if (M == 0) return BS_OK;
+  if (!x || !weight || !A || !As) return BS_ERR_ARG;
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(A) || (residual && !aligned16(residual))) return BS_ERR_ALIGN;
+  if (K > bs::kNormThreads * 8 * bs::kNormMaxRounds) return BS_ERR_ARG;
+  if (!device_state()) return BS_ERR_CUDA;
+  // registers scale with the chunks each thread holds, so the kernel is built per round count
+  const int rounds = (K / 8 + bs::kNormThreads - 1) / bs::kNormThreads;
+  auto kern = rounds <= 1 ? bs::k_rmsnorm_group_quant<1>
+              : rounds <= 2 ? bs::k_rmsnorm_group_quant<2>
+              : rounds <= 3 ? bs::k_rmsnorm_group_quant<3>
+              : rounds <= 4 ? bs::k_rmsnorm_group_quant<4>
+                            : bs::k_rmsnorm_group_quant<8>;
+  return launch_pdl(kern, M, bs::kNormThreads, 0, static_cast<cudaStream_t>(stream), "k_rmsnorm_group_quant launch",
+                    static_cast<const __nv_bfloat16*>(x), ldx, static_cast<__nv_bfloat16*>(residual), ldr,
+                    static_cast<const __nv_bfloat16*>(weight), eps, static_cast<uint8_t*>(A), As, M, K);
+}
+
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {
   if (N <= 0 || K <= 0 || N % 128 || K % 128) return BS_ERR_ARG;
   if (!W || !tiles) return BS_ERR_ARG;

@@ -53,6 +53,36 @@ def group_quant(x: torch.Tensor, group_size: int = BLOCK) -> tuple[torch.Tensor,
     return A.view(*x.shape[:-1], K), As.view(*x.shape[:-1], K // BLOCK)
 
 
+def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                        residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm fused with the per-token-group quant of its output (the next linear's activation quant):
+    h = x, or h = bf16(x + residual) stored into `residual` in place (fused add); y = bf16(h * rsqrt(mean(h^2)
+    + eps) * weight); returns group_quant(y) = (A e4m3 [..., K], As fp32 [..., K/128]) without storing y."""
+    _need(x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16, "x and weight must be bf16")
+    dev = _cuda(x, weight) if residual is None else _cuda(x, weight, residual)
+    K = x.shape[-1]
+    _need(K % BLOCK == 0, "K must be a multiple of 128")
+    _need(weight.shape == (K,) and weight.is_contiguous(), "weight must be contiguous [K]")
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    r_ptr, ldr = None, K
+    if residual is not None:
+        _need(residual.dtype == torch.bfloat16 and residual.shape == x.shape, "residual must be bf16 like x")
+        r2 = residual.view(-1, K)
+        _need(r2.stride(-1) == 1 and r2.stride(0) % 8 == 0 and r2.data_ptr() % 16 == 0,
+              "residual rows must be contiguous and 16-byte aligned (it is updated in place)")
+        r_ptr, ldr = r2.data_ptr(), r2.stride(0)
+    A = torch.empty((M, K), dtype=E4M3, device=dev)
+    As = torch.empty((M, K // BLOCK), dtype=torch.float32, device=dev)
+    with _native.device_guard(dev):
+        _native.check(_native.lib().bs_fp8_rmsnorm_group_quant(
+            x2.data_ptr(), x2.stride(0), r_ptr, ldr, weight.data_ptr(), float(eps), A.data_ptr(), As.data_ptr(),
+            M, K, _native.stream_handle(dev)), "bs_fp8_rmsnorm_group_quant")
+    return A.view(*x.shape[:-1], K), As.view(*x.shape[:-1], K // BLOCK)
+
+
 def pack_tiles(weight: torch.Tensor) -> torch.Tensor:
     """e4m3 weight [N, K] -> tile-first bytes [N/128, K/128, 128, 128] (H:667 layout)."""
     _need(weight.dim() == 2 and weight.dtype in (E4M3, torch.uint8), "weight must be e4m3 [N, K]")
