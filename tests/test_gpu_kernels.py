@@ -74,6 +74,45 @@ def test_rmsnorm_group_quant_bit_exact(cuda_lib, M, K, fused_add):
         assert torch.equal(rd.cpu(), h_ref)
 
 
+@pytest.mark.parametrize("fused", ["1", "0"])
+def test_mlp_takes_fused_norm_output(cuda_lib, monkeypatch, fused):
+    """Decoder-layer chain norm -> MLP through the drop-in API: GatedMLP takes the (A, As) pair of the fused
+    norm kernel as its input, on the fused gate_up path and on the unfused fallback."""
+    import importlib
+    monkeypatch.setenv("SGLANG_FP8_HAND_GEMM", "1")
+    monkeypatch.setenv("SGLANG_FP8_HAND_FUSED", fused)
+    from fp8_hand_b200 import fp8_hand_sm100, sglang_compat
+    importlib.reload(fp8_hand_sm100)
+    try:
+        M, H, inter = 200, 512, 1024
+        gu, gus = O.make_weight(2 * inter, H, seed=21)
+        dn, dns = O.make_weight(H, inter, seed=22)
+        mlp = sglang_compat.GatedMLP(sglang_compat.Fp8BlockLinear(gu.cuda(), gus.cuda()),
+                                     sglang_compat.Fp8BlockLinear(dn.cuda(), dns.cuda()))
+        sglang_compat.post_load(mlp)
+        g = torch.Generator().manual_seed(23)
+        x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+        A, As = _ops().rmsnorm_group_quant(x.cuda(), w.cuda(), 1e-6)
+        out = mlp((A, As)).cpu()
+        A_ref, As_ref, _ = O.rmsnorm_group_quant(x, w, 1e-6)
+        # the fallback rounds gate_up to bf16 before SiLU * up and the quant: the oracle's unfused chain
+        front = O.fused_gate_up if fused == "1" else O.chain_gate_up
+        Q_ref, Qs_ref, _ = front(A_ref, gu, As_ref, gus)
+        ref = O.blockwise_matmul(Q_ref, dn, Qs_ref, dns)
+        assert out.shape == (M, H) and out.dtype == torch.bfloat16
+        assert O.norm_rel_error(out.float(), ref.float()) <= 1e-2
+        if fused == "1":
+            # the tuple goes straight into the fused kernel: same bytes as calling the ops by hand
+            Q, Qs = _ops().gemm_silu_quant(A, mlp.gate_up_proj.weight.tiles, As, gus.cuda(), b_tiled=True)
+            direct = _ops().gemm(Q, mlp.down_proj.weight.tiles, Qs, dns.cuda(), b_tiled=True)
+            assert torch.equal(out, direct.cpu())
+    finally:
+        monkeypatch.delenv("SGLANG_FP8_HAND_FUSED")
+        monkeypatch.delenv("SGLANG_FP8_HAND_GEMM")
+        importlib.reload(fp8_hand_sm100)
+
+
 def test_rmsnorm_group_quant_strided_rows(cuda_lib):
     x = torch.randn(9, 384, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
     w = torch.ones(256, dtype=torch.bfloat16)

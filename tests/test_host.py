@@ -152,6 +152,9 @@ def test_dropin_fallback_contract(monkeypatch):
     assert m.fused_gate_up(_Proj(512, 256, tiles=False), torch.zeros(64, 256, dtype=torch.bfloat16)) is None
     assert m.fused_gate_up(_Proj(384, 256), torch.zeros(64, 256, dtype=torch.bfloat16)) is None  # N % 256
     assert m.fused_gate_up(_Proj(512, 256), torch.zeros(64, 256)) is None  # not bf16
+    q8 = torch.zeros(8, 256, dtype=torch.float8_e4m3fn)
+    assert m.fused_gate_up(_Proj(512, 256), (q8, torch.ones(8, 2))) is None  # pre-quantised, M < FUSED_MIN_M
+    assert m.fused_gate_up(_Proj(512, 256), (q8.view(torch.uint8), torch.ones(8, 2))) is None  # not e4m3
     w = torch.empty(256, 256, dtype=torch.float8_e4m3fn)
     assert m.matmul(None, w, None, None, None, 8, 256, 256, [128, 128]) is False
     m = _fresh_module(monkeypatch, SGLANG_FP8_HAND_GEMM="1", SGLANG_FP8_HAND_FUSED="0")

@@ -96,9 +96,22 @@ def relayout(model: torch.nn.Module) -> None:
     logger.info("FP8 hand: %d linears tile first", moved)
 
 
-def fused_gate_up(proj, x: torch.Tensor):
-    """Returns (q, scale) for down_proj, or None to run the separate kernels (H:675-701)."""
-    if not FUSED_ENABLED or x.dtype != torch.bfloat16 or x.ndim != 2 or x.shape[0] < FUSED_MIN_M:
+def fused_gate_up(proj, x):
+    """Returns (q, scale) for down_proj, or None to run the separate kernels (H:675-701).
+
+    x is the bf16 activation [M, K], or an already quantised (A e4m3 [M, K], As fp32 [M, K/128]) pair, e.g.
+    from ops.rmsnorm_group_quant, in the (fp8, scale) tuple form the reference hands between its hooks
+    (patches/apply_sglang_gdn_prefill.py:578-589)."""
+    pre = isinstance(x, tuple)
+    if pre:
+        if len(x) != 2 or x[0].dtype != torch.float8_e4m3fn or x[0].ndim != 2:
+            return None
+        rows = x[0].shape[0]
+    else:
+        if x.dtype != torch.bfloat16 or x.ndim != 2:
+            return None
+        rows = x.shape[0]
+    if not FUSED_ENABLED or rows < FUSED_MIN_M:
         return None
     weight = getattr(proj, "weight", None)
     scale = getattr(proj, "weight_scale_inv", None)
@@ -108,7 +121,7 @@ def fused_gate_up(proj, x: torch.Tensor):
     N, K = weight.shape
     if K % BK or N % (2 * BK) or getattr(proj, "bias", None) is not None:
         return None
-    A, As = ops.group_quant(x, BK)
+    A, As = x if pre else ops.group_quant(x, BK)
     return ops.gemm_silu_quant(A, tiles, As, scale, b_tiled=True)
 
 
