@@ -1,7 +1,8 @@
-"""GPU: the prefill kernel on CTA pairs (cta_group::2, 256-row tiles), which the library uses only when
-BS_FP8_PAIR_MIN_ROWS is set. The prefill GEMM and fused cases of test_gpu_kernels.py run again in a child
-process with the variable set, so every pair tile shape there (full, last tile with 8 valid rows, last tile
-whose second CTA holds no valid row, half-empty last column tile) is checked against the oracle."""
+"""GPU: the prefill kernel on CTA pairs (cta_group::2, 256-row tiles). By default the library uses it for the
+fused kernel from 1024 rows only; here the prefill GEMM and fused cases of test_gpu_kernels.py run again in a
+child process with BS_FP8_PAIR_MIN_ROWS=512, so every pair tile shape there (full, last tile with 8 valid rows,
+last tile whose second CTA holds no valid row, half-empty last column tile) and the plain GEMM on pairs are
+checked against the oracle."""
 import os
 import subprocess
 import sys

@@ -108,20 +108,26 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int ntp_for(int M) { return ((M + 15) / 16) * 16; }
 
-// Prefill row count from which 256-row tiles on CTA pairs (cta_group::2) are used. Off unless the
-// environment sets BS_FP8_PAIR_MIN_ROWS (read once per process): the pair kernel is exact but measured
-// slower than one CTA per tile, because each K block's promotion handoff then crosses the pair.
-int pair_min_rows() {
+// Prefill row count from which 256-row tiles on CTA pairs (cta_group::2) are used. Measured on B200
+// (K = 5120): the fused gate_up kernel is faster on pairs from M = 1024 (8192 rows: 1891 vs 1826
+// TFLOP/s), where each CTA stages 32 KB per K block instead of 48 KB; the plain GEMM is slower on pairs
+// (1716 vs 1938), so it stays on one CTA per tile. BS_FP8_PAIR_MIN_ROWS, read once per process,
+// replaces both thresholds (a very large value turns pairs off).
+int pair_min_rows(bool fused) {
+  struct Rows {
+    int fused = 1024;
+    int plain = 0x7fffffff;
+  };
   static std::once_flag once;
-  static int rows = 0x7fffffff;
+  static Rows rows;
   std::call_once(once, [] {
     const char* v = std::getenv("BS_FP8_PAIR_MIN_ROWS");
     if (v && *v) {
       const long r = std::strtol(v, nullptr, 10);
-      if (r > 0 && r < 0x7fffffff) rows = static_cast<int>(r);
+      if (r > 0 && r <= 0x7fffffff) rows.fused = rows.plain = static_cast<int>(r);
     }
   });
-  return rows;
+  return fused ? rows.fused : rows.plain;
 }
 
 // Grid of the decode kernels. When the weight tiles nearly match the SM count (>= 90%), one CTA
@@ -341,7 +347,7 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
   const int num_n = fused ? N / 256 : (N / 128 + 1) / 2;
   // 256-row tiles on CTA pairs once there are enough rows for them
-  const bool pair = M >= pair_min_rows();
+  const bool pair = M >= pair_min_rows(fused);
   const int rows = pair ? 256 : 128;
   const int num_m = (M + rows - 1) / rows;
   // Raster: one group over every M tile when the whole A panel stays in L2 (each weight tile is then

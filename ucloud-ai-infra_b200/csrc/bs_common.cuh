@@ -90,39 +90,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Same contract as mbar_wait, but polls with the non-suspending test_wait: for the MMA <-> promotion
-// handoffs, where a suspended waiter's wake-up latency sits on the critical path of every K block.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
-                                               int code, uint64_t limit_ns = kWaitLimitNs) {
-  if (mbar_test_wait(bar, parity)) return true;
-  if (*abort) return false;
-  const uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
-  while (true) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((++spins & 1023u) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
-        atomicCAS(status, 0, code);
-        *abort = 1;
-        return false;
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------- TMA (per-CTA, never multicast)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -136,6 +103,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// Pair form (cta_group::2, no multicast): the box lands in this CTA's shared memory and its bytes
+// are counted on the barrier at shared::cluster address `bar_cluster`, which may be the peer CTA's.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 
@@ -238,8 +216,16 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
   return d;
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Relaxed remote arrival: the count only, no memory ordering. Hands a TMEM buffer back after
+// tcgen05.wait::ld (the loads have completed; nothing this thread wrote needs to be seen).
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Busy-waits `ns` nanoseconds of wall time.
+__device__ __forceinline__ void pause_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
 }
 // Every thread of both CTAs; orders all earlier shared-memory and barrier work cluster-wide.
 __device__ __forceinline__ void cluster_sync_all() {
@@ -275,12 +261,6 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask
       : "memory");
 }
 
-// Arrive once on the barrier at shared::cluster address `bar` (possibly the peer's) when this thread's
-// pair MMAs so far have completed; with none pending it arrives at once.
-__device__ __forceinline__ void mma_commit_pair_to(uint32_t bar_cluster_addr) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
-               : "memory");
-}
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

@@ -83,6 +83,15 @@ __device__ __forceinline__ void load_weight_box(void* dst, const CUtensorMap* ma
     tma_load_2d(dst, map, bar, kb * 128, nb * 128, policy);
 }
 
+// Pair form: the box's bytes are counted on the leader's barrier at shared::cluster address `bar`.
+__device__ __forceinline__ void load_weight_box_pair(void* dst, const CUtensorMap* map, uint32_t bar, int nb, int kb,
+                                                     int KB, int tiled, uint64_t policy) {
+  if (tiled)
+    tma_load_2d_pair(dst, map, bar, 0, (nb * KB + kb) * 128, policy);
+  else
+    tma_load_2d_pair(dst, map, bar, kb * 128, nb * 128, policy);
+}
+
 __device__ __forceinline__ void prefetch_weight_box(const CUtensorMap* map, int nb, int kb, int KB, int tiled) {
   if (tiled)
     tma_prefetch_l2_2d(map, 0, (nb * KB + kb) * 128);
@@ -110,13 +119,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Pair: rank 0 (leader) issues the MMAs for both CTAs; rank 1 forwards "stage landed" to it and
-  // releases TMEM buffers on its barriers.
+  // Pair: rank 0 (leader) issues the MMAs for both CTAs; both CTAs' TMA loads count their bytes on
+  // the leader's full barriers, and the peer hands TMEM buffers back on the leader's barriers.
   const uint32_t cr = PAIR ? cluster_ctarank() : 0u;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], (PAIR && cr == 0) ? 2 : 1);  // leader: own producer + peer's forwarder
+      mbar_init(&full[i], 1);  // the (leader's) producer's arrive.expect_tx
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -182,11 +191,16 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
           }
           BS_TR_ADD(0);
           uint8_t* st = smem + s * Cfg::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          tma_load_2d(st, &tmA, &full[s], kb * 128, tm * Cfg::kRows + row0, pol_a);
           if constexpr (PAIR) {
-            load_weight_box(st + Cfg::kABytes, &tmB, &full[s], cr == 0 ? nb0 : nb1, kb, KB, p.b_tiled, pol_b);
+            // The leader expects both CTAs' bytes; the peer's loads may land before that, which only
+            // takes the transaction count below zero until the leader's arrival.
+            const uint32_t lead_full = mapa_shared(&full[s], 0);
+            if (cr == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+            tma_load_2d_pair(st, &tmA, lead_full, kb * 128, tm * Cfg::kRows + row0, pol_a);
+            load_weight_box_pair(st + Cfg::kABytes, &tmB, lead_full, cr == 0 ? nb0 : nb1, kb, KB, p.b_tiled, pol_b);
           } else {
+            mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+            tma_load_2d(st, &tmA, &full[s], kb * 128, tm * Cfg::kRows, pol_a);
             load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
             load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
           }
@@ -200,10 +214,16 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
       }
       BS_TR_FLUSH(0, 1);
       if (!ok) {
-        // Leave no copy in flight: wait (bounded) for the last fill of every stage.
-        for (int i = 0; i < S; ++i)
-          if (issued & (1u << i))
-            mbar_wait(&full[i], (parity_bits >> i) & 1u, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
+        if constexpr (PAIR) {
+          // The copies complete on the leader's barrier, which the peer cannot observe and which also
+          // waits for the other CTA's bytes: give them time to land (they take microseconds).
+          pause_ns(2000000ull);
+        } else {
+          // Leave no copy in flight: wait (bounded) for the last fill of every stage.
+          for (int i = 0; i < S; ++i)
+            if (issued & (1u << i))
+              mbar_wait(&full[i], (parity_bits >> i) & 1u, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
+        }
       }
     }
   } else if (warp == 9) {
@@ -263,29 +283,6 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
         mma_commit(drain);
       mbar_wait(drain, 0, abort_flag, p.status, kErrTimeoutDrain, 100000000ull);
     }
-  } else if (PAIR && warp == 10 && cr == 1) {
-    // ------------------------------------------------------------ stage forwarder (pair peer)
-    // The peer's TMA loads complete on its own full barrier (so an aborting CTA can drain its own
-    // copies); this warp passes each completed stage on to the leader's full barrier.
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      for (int tile = tile0; tile < num_tiles; tile += tstep) {
-        bool ok = true;
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_remote(mapa_shared(&full[s], 0));
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
-          }
-        }
-        if (!ok) break;
-      }
-    }
   }
   } else {
     regs_increase<Cfg::Regs::kConsumer>();
@@ -295,6 +292,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     const int q = warp & 3;           // TMEM lane quarter
     const int r = q * 32 + lane;      // row inside the tile
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t lead_pempty = PAIR ? mapa_shared(&pempty[0], 0) : 0u;  // the leader's pempty[0]
     // After an abort these warps keep walking the tile loop (skipping every wait, TMEM read and
     // store) so that both warpgroups still meet at the same named barriers.
     int b = 0;
@@ -345,11 +343,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
           if (!PAIR || cr == 0) {
             mbar_arrive(&pempty[b]);
           } else {
-            // The leader's MMA reuses it: one arrival per warp on the leader's barrier, sent with a pair
-            // commit (no MMA of this thread is pending, so it arrives at once); measured much faster
-            // than a cluster-scope release arrive.
+            // The leader's MMA reuses it: one relaxed arrival per warp on the leader's barrier (a
+            // cluster-scope release arrival here costs a fence per K block on the critical path).
             __syncwarp();
-            if (lane == 0) mma_commit_pair_to(mapa_shared(&pempty[b], 0));
+            if (lane == 0) {
+              tc_fence_before();
+              mbar_arrive_remote_relaxed(lead_pempty + 8u * static_cast<uint32_t>(b));
+            }
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
