@@ -55,7 +55,7 @@ def test_group_quant_strided_rows(cuda_lib):
 
 
 @pytest.mark.parametrize("M,K,fused_add", [(1, 128, False), (7, 640, True), (300, 5120, False), (33, 5120, True),
-                                            (64, 16384, True)])
+                                            (64, 16384, True), (2049, 1024, True), (2048, 5120, False)])
 def test_rmsnorm_group_quant_bit_exact(cuda_lib, M, K, fused_add):
     """Fused RMSNorm + group quant against the oracle restatement (same rounding points and summation
     order): e4m3 bytes, scales and the updated residual all bit-exact."""

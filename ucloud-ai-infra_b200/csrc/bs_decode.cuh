@@ -428,9 +428,11 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
               for (int i = 0; i < TR; ++i)
                 if (tok0 + i < M) part[(w * NTP + tok0 + i) * 128] = pair_elem(acc[w][i / 2], i & 1);
           }
-          __threadfence();
+          // Release: the barrier orders every promotion thread's partial stores before thread 0's
+          // device-scope fence, which makes them visible before the counter increment.
           named_bar_sync(1, NPROMO);
           if (tid == 0) {
+            __threadfence();
             const int prev = atomicAdd(&p.cnt[t], 1);
             const int last = prev == c_last - c_first;
             if (last) p.cnt[t] = 0;
