@@ -113,6 +113,43 @@ def test_mlp_takes_fused_norm_output(cuda_lib, monkeypatch, fused):
         importlib.reload(fp8_hand_sm100)
 
 
+def test_relayout_reads_tile_cache(cuda_lib, monkeypatch, tmp_path):
+    """relayout(model, cache): the first call packs and writes the tile-pack file; a model whose row-major
+    weights were never loaded (meta device) gets the same tiles from it and the same MLP output; a file
+    whose block scales do not match the model is refused."""
+    import importlib
+    monkeypatch.setenv("SGLANG_FP8_HAND_GEMM", "1")
+    from fp8_hand_b200 import fp8_hand_sm100, sglang_compat, tilepack
+    importlib.reload(fp8_hand_sm100)
+    try:
+        H, inter = 512, 1024
+        gu, gus = O.make_weight(2 * inter, H, seed=31)
+        dn, dns = O.make_weight(H, inter, seed=32)
+
+        def mlp_of(gw, dw, scale_mult=1.0):
+            return sglang_compat.GatedMLP(sglang_compat.Fp8BlockLinear(gw, (gus * scale_mult).cuda()),
+                                          sglang_compat.Fp8BlockLinear(dw, dns.cuda()))
+
+        def meta(n, k):
+            return torch.empty(n, k, dtype=torch.float8_e4m3fn, device="meta")
+
+        cache = tmp_path / "mlp.bsfp8"
+        a = mlp_of(gu.cuda(), dn.cuda())
+        sglang_compat.post_load(a, cache=cache)
+        assert set(tilepack.read_header(cache)["entries"]) == {"gate_up_proj", "down_proj"}
+        b = mlp_of(meta(2 * inter, H), meta(H, inter))
+        sglang_compat.post_load(b, cache=cache)
+        for m in ("gate_up_proj", "down_proj"):
+            assert torch.equal(getattr(a, m).weight.tiles, getattr(b, m).weight.tiles)
+        x = O.make_activation(200, H, seed=33).cuda()
+        assert torch.equal(a(x), b(x))
+        with pytest.raises(tilepack.TilePackError):
+            sglang_compat.post_load(mlp_of(meta(2 * inter, H), meta(H, inter), scale_mult=2.0), cache=cache)
+    finally:
+        monkeypatch.delenv("SGLANG_FP8_HAND_GEMM")
+        importlib.reload(fp8_hand_sm100)
+
+
 def test_rmsnorm_group_quant_strided_rows(cuda_lib):
     x = torch.randn(9, 384, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
     w = torch.ones(256, dtype=torch.bfloat16)

@@ -8,7 +8,8 @@ import this module instead:
                                           SGLANG_FP8_HAND_FUSED_MIN_M (H:41-43)
   select(N, M) -> dict                    tile choice of an M x N product (H:74-81)
   precompile() -> list[str]               build step, never on the request path (H:596-611)
-  relayout(model)                         tile-first weight pre-pack after loading (H:652-672)
+  relayout(model, cache=None)             tile-first weight pre-pack after loading (H:652-672); with a
+                                          cache file (tilepack.py) the packed tiles are read, not permuted
   fused_gate_up(proj, x) -> (Q, Qs)|None  fused MLP front half (H:675-701)
   matmul(A, B, C, As, Bs, M, N, K, block_size) -> bool   GEMM hook (H:704-719)
 
@@ -29,7 +30,7 @@ import os
 import torch
 from torch.nn import Parameter
 
-from . import _build, _native, ops
+from . import _build, _native, ops, tilepack
 
 logger = logging.getLogger(__name__)
 
@@ -72,12 +73,18 @@ def eligible(name: str, weight: torch.Tensor, scale: torch.Tensor | None) -> boo
     return N % BK == 0 and K % BK == 0 and tuple(scale.shape) == (N // BK, K // BK)
 
 
-def relayout(model: torch.nn.Module) -> None:
+def relayout(model: torch.nn.Module, cache: str | os.PathLike | None = None) -> None:
     """Moves every eligible FP8 linear to tile-first storage. The parameter keeps its shape on the
-    meta device, so nothing can read the old layout by accident (H:652-672)."""
+    meta device, so nothing can read the old layout by accident (H:652-672).
+
+    cache: a tile-pack file (tilepack.py). Entries it holds are read from it instead of being packed, so
+    their row-major weights need not be loaded at all (a weight on the meta device is fine); their block
+    scales must equal the module's weight_scale_inv. If the file does not exist, the packed weights are
+    written to it."""
     if not ENABLED or not _is_b200():
         return
-    moved = 0
+    stored = tilepack.read_header(cache)["entries"] if cache is not None and os.path.exists(cache) else None
+    todo = []
     for name, module in model.named_modules():
         weight = getattr(module, "weight", None)
         scale = getattr(module, "weight_scale_inv", None)
@@ -87,13 +94,31 @@ def relayout(model: torch.nn.Module) -> None:
             if isinstance(weight, torch.Tensor) and weight.dtype == torch.float8_e4m3fn:
                 logger.info("FP8 hand: %s %s stays on the row-major path", name, tuple(weight.shape))
             continue
-        N, K = weight.shape
-        tiles = ops.pack_tiles(weight.data)
+        todo.append((name, module))
+    cached = {}
+    if stored is not None:
+        names = [name for name, module in todo
+                 if name in stored and (stored[name]["N"], stored[name]["K"]) == tuple(module.weight.shape)]
+        if names:
+            cached = tilepack.load(cache, device=todo[0][1].weight_scale_inv.device, names=names)
+    packed = {}
+    for name, module in todo:
+        N, K = module.weight.shape
+        if name in cached:
+            tiles, scale = cached.pop(name)
+            if not torch.equal(scale, module.weight_scale_inv.data):
+                raise tilepack.TilePackError(f"{name}: block scales in {cache} differ from the loaded weight_scale_inv")
+        else:
+            if module.weight.device.type == "meta":
+                raise tilepack.TilePackError(f"{name}: weight not loaded and not in the tile cache {cache}")
+            tiles = ops.pack_tiles(module.weight.data)
+            packed[name] = (tiles, module.weight_scale_inv.data)
         module.weight = Parameter(torch.empty(N, K, dtype=torch.float8_e4m3fn, device="meta"), requires_grad=False)
         module.weight.tiles = tiles
-        moved += 1
+    if cache is not None and stored is None and packed:
+        tilepack.save(cache, packed)
     torch.cuda.empty_cache()
-    logger.info("FP8 hand: %d linears tile first", moved)
+    logger.info("FP8 hand: %d linears tile first (%d from %s)", len(todo), len(todo) - len(packed), cache)
 
 
 def fused_gate_up(proj, x):

@@ -89,6 +89,7 @@ class GatedMLP(nn.Module):
         return x
 
 
-def post_load(model: nn.Module) -> None:
-    """Loader post-hook (apply_sglang_fp8_hand_gemm.py:59-65): tile-first pre-pack."""
-    fp8_hand.relayout(model)
+def post_load(model: nn.Module, cache=None) -> None:
+    """Loader post-hook (apply_sglang_fp8_hand_gemm.py:59-65): tile-first pre-pack, read from the
+    tile-pack file `cache` when it exists (written there otherwise)."""
+    fp8_hand.relayout(model, cache=cache)
