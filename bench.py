@@ -232,7 +232,7 @@ def fp8_peak_tflops(device) -> float:
 
 
 # ----------------------------------------------------------------------------- our arm
-def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS):
+def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="multimem"):
     from fp8_hand_b200 import fp8_hand_sm100, sglang_compat, tp
     gu_q, gu_s, dn_q, dn_s = make_weights(device)
     if world == 1:
@@ -243,15 +243,22 @@ def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS):
         return (mlp, (mlp.gate_up_proj.weight.tiles, gu_s), (mlp.down_proj.weight.tiles, dn_s), 2 * INTER)
     shard = tp.make_shard(gu_q, gu_s, dn_q, dn_s, rank, world, device=device, tiled=True)
     del gu_q, dn_q
-    return (tp.TensorParallelMLP(shard, chunks=tp_chunks), (shard.gate_up, shard.gate_up_scale),
-            (shard.down, shard.down_scale),
-            2 * INTER // world)
+    mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce)
+    if tp_reduce == "multimem":
+        try:
+            mlp.multicast_out(M_PREFILL, HIDDEN, device)  # collective; every rank sees the same outcome
+        except RuntimeError as e:
+            if rank == 0:
+                print(f"bench: multicast reduction unavailable ({e}); using the NCCL all_reduce", file=sys.stderr)
+            mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks)
+    return (mlp, (shard.gate_up, shard.gate_up_scale), (shard.down, shard.down_scale), 2 * INTER // world)
 
 
 def run_ours(args, rank, world, device) -> dict | None:
     from fp8_hand_b200 import ops
     torch.cuda.set_device(device)
-    mlp, (gu_tiles, gu_s), (dn_tiles, dn_s), n2_local = build_mlp(rank, world, device, args.tp_chunks)
+    mlp, (gu_tiles, gu_s), (dn_tiles, dn_s), n2_local = build_mlp(rank, world, device, args.tp_chunks,
+                                                                  args.tp_reduce)
     x = make_x(M_PREFILL, device)
     stream = torch.cuda.current_stream(device)
 
@@ -411,9 +418,12 @@ def run_ours(args, rank, world, device) -> dict | None:
         "config": {
             "workload": "config[2] MLP at M=8192: group quant -> fused gate_up+SiLU*up+quant (K=5120, N2=34816) "
                         "-> down_proj (K=17408, N=5120), bf16 in/out" +
-                        (f"; config[4] tensor-parallel tp={world}, bf16 partials + NCCL all_reduce"
-                         + (f" in {args.tp_chunks} row chunks overlapped with compute, GEMM grids on "
-                            f"{os.environ.get('BS_FP8_SM_LIMIT', 'all')} SMs" if args.tp_chunks > 1 else "")
+                        ((f"; config[4] tensor-parallel tp={world}, bf16 partials added into every rank's "
+                          "output by the down_proj epilogue through NVSwitch multicast (multimem.red), no "
+                          "separate collective") if getattr(mlp, "reduce", "nccl") == "multimem" else
+                         (f"; config[4] tensor-parallel tp={world}, bf16 partials + NCCL all_reduce"
+                          + (f" in {args.tp_chunks} row chunks overlapped with compute, GEMM grids on "
+                             f"{os.environ.get('BS_FP8_SM_LIMIT', 'all')} SMs" if args.tp_chunks > 1 else ""))
                          if world > 1 else ""),
             "M": M_PREFILL, "hidden": HIDDEN, "intermediate": INTER, "parallelism": f"tp{world}",
             "l2": "inputs larger than L2 (weights 267 MB + x 84 MB per step vs 126 MB L2)",
@@ -521,6 +531,9 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--tp-chunks", type=int, default=TP_CHUNKS,
                     help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
+    ap.add_argument("--tp-reduce", choices=("multimem", "nccl"), default="nccl",
+                    help="N > 1: sum the down_proj partials in its epilogue through NVSwitch multicast "
+                         "(falls back to NCCL where the group has no multicast mapping) or with NCCL")
     ap.add_argument("--ref-rows", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -66,6 +66,19 @@ int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* A
                            int M, int N2, int K, int b_tiled, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* bs_fp8_gemm for a row-parallel layer of a tensor-parallel group, fused with the group's reduction:
+ * C_mc is the multicast address (NVLink SHARP / NVLS, one buffer mapped on every rank of the group) of
+ * a bf16 [M, ldc] output, and every output tile this rank computes is added, in bf16 by the switch, into
+ * all ranks' copies (multimem.red.add). Replaces the NCCL all_reduce(sum) of the bf16 partials that
+ * follows the row-parallel down_proj (the reference runs one GPU, scripts/run_sglang_48g.sh:117: there
+ * the product is the whole sum). The caller zeroes every rank's copy and synchronises the group before
+ * the call, and synchronises the group again before reading C. The order in which ranks' additions land
+ * is not fixed, so the last bits of C may differ from run to run. Same arguments, workspace rule and
+ * status codes as bs_fp8_gemm with out_dtype 0. */
+int bs_fp8_gemm_reduce_multicast(const void* A, const void* B, void* C_mc, const float* As, const float* Bs, int M,
+                                 int N, int K, int ldc, int b_tiled, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* Allocation-free variant of bs_fp8_gemm, for callers that cannot call cudaMalloc (an engine that
  * reserves all device memory up front, an embedding whose only allocator is its own arena, a
  * thread that must not block on the driver's allocator). No counterpart in the reference.

@@ -15,6 +15,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 H, INTER, M = 1024, 2048, 200
+M_DECODE = 56
 
 
 def _free_port():
@@ -49,8 +50,14 @@ def _worker(rank, world, port, q):
         outs = (tp.TensorParallelMLP(shard)(xd),                                  # bf16 partials (config 4)
                 tp.TensorParallelMLP(shard, partial_dtype=torch.float32)(xd),     # fp32 partials
                 tp.TensorParallelMLP(shard, chunks=2)(xd))                        # overlapped row chunks
+        # down_proj fused with the sum through NVSwitch multicast: prefill (200 rows) and decode (56 rows)
+        try:
+            mlp_mc = tp.TensorParallelMLP(shard, reduce="multimem")
+            mc = (mlp_mc(xd).clone(), mlp_mc(xd[:M_DECODE].contiguous()).clone())
+        except RuntimeError as e:  # no multicast mapping on this box: every rank raises the same
+            mc = str(e)
         torch.cuda.synchronize()
-        q.put((rank, tuple(o.cpu() for o in outs)))
+        q.put((rank, tuple(o.cpu() for o in outs), mc if isinstance(mc, str) else tuple(o.cpu() for o in mc)))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -64,6 +71,9 @@ def test_tp2_matches_single_gpu():
     A, As = ops.group_quant(x.cuda())
     Q, Qs = ops.gemm_silu_quant(A, gu.cuda(), As, gus.cuda())
     single = ops.gemm(Q, dn.cuda(), Qs, dns.cuda(), out_dtype=torch.float32).to(torch.bfloat16).cpu()
+    A, As = ops.group_quant(x[:M_DECODE].cuda())
+    Q, Qs = ops.gemm_silu_quant(A, gu.cuda(), As, gus.cuda())
+    single_dec = ops.gemm(Q, dn.cuda(), Qs, dns.cuda(), out_dtype=torch.float32).cpu()
 
     world = 2
     ctx = mp.get_context("spawn")
@@ -72,10 +82,12 @@ def test_tp2_matches_single_gpu():
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    outs = dict(q.get(timeout=300) for _ in range(world))
+    got = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    outs = {r: o for r, o, _ in got}
+    mcs = {r: m for r, _, m in got}
     for k in range(3):
         assert torch.equal(outs[0][k], outs[1][k])
     out_bf16, out_f32, out_chunked = outs[0]
@@ -90,3 +102,12 @@ def test_tp2_matches_single_gpu():
     # row chunks (the 72-row tail runs the decode kernels, whose split-K sums in another order)
     assert (out_chunked.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
     assert O.norm_rel_error(out_chunked.float(), ref) <= 4e-3
+    # multicast reduction: bf16 partials added in bf16 by the switch, in no fixed order of ranks, so each
+    # rank's copy is checked against the single-GPU result with the bf16-partial bound
+    if isinstance(mcs[0], str):
+        pytest.skip(f"NVSwitch multicast unavailable: {mcs[0]}")
+    for r in range(world):
+        mc_pre, mc_dec = mcs[r]
+        for got_r, want in ((mc_pre, ref), (mc_dec, single_dec)):
+            assert (got_r.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+            assert O.norm_rel_error(got_r.float(), want) <= 4e-3

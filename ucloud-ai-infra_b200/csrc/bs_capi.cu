@@ -289,9 +289,10 @@ int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::Gem
   return launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, s, "k_prefill launch", tmA, tmB, p);
 }
 
-// Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant.
+// Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant / bs_fp8_gemm_reduce_multicast.
 int run_gemm(bool fused, const void* A, const void* B, void* out, const float* As, const float* Bs, float* qs,
-             int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream) {
+             int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream,
+             int out_mc = 0) {
   if (M < 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0) return BS_ERR_ARG;
   if (fused && N % 256 != 0) return BS_ERR_ARG;
   if (!fused && (ldc < N || ldc % 8 != 0 || (out_dtype != 0 && out_dtype != 1))) return BS_ERR_ARG;
@@ -312,6 +313,7 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   p.ldc = fused ? N / 2 : ldc;
   p.b_tiled = b_tiled;
   p.out_f32 = fused ? 0 : out_dtype;
+  p.out_mc = out_mc;
 
   p.As = As;
   p.Bs = Bs;
@@ -443,6 +445,13 @@ int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, 
                     kNoAllocScratchBytes, stream);
   }
   return run_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype, nullptr, 0, stream);
+}
+
+int bs_fp8_gemm_reduce_multicast(const void* A, const void* B, void* C_mc, const float* As, const float* Bs, int M,
+                                 int N, int K, int ldc, int b_tiled, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  return run_gemm(false, A, B, C_mc, As, Bs, nullptr, M, N, K, ldc, b_tiled, 0, workspace, workspace_bytes, stream,
+                  1);
 }
 
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {

@@ -221,6 +221,20 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Tensor-parallel reductions through NVSwitch: `mc` is a multicast address (the same buffer mapped on
+// every rank); the switch adds the values into each rank's copy (bf16 arithmetic, any order of ranks).
+__device__ __forceinline__ void multimem_add_bf16x8(void* mc, const uint4& v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_add_bf16x2(void* mc, uint32_t v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.bf16x2 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+// Orders this thread's earlier memory operations, multimem ones included, before its later ones at
+// system scope.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // Busy-waits `ns` nanoseconds of wall time.
 __device__ __forceinline__ void pause_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer_ns();

@@ -464,8 +464,21 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
         }
         if (finisher) {
           if constexpr (!FUSED) {
-            if (ok) {
-              const size_t col = static_cast<size_t>(t) * 128 + r;
+            const size_t col = static_cast<size_t>(t) * 128 + r;
+            if (p.out_mc) {
+              // Tensor-parallel partial added into every rank's output through the switch. The reduction
+              // is 4 bytes wide, so an even row r sends the column pair (r, r + 1); lane r + 1 of the same
+              // warp holds r + 1. Every lane takes part in the shuffle, whatever its `ok`.
+              __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.out) + col;
+#pragma unroll
+              for (int i = 0; i < TR; ++i) {
+                const float v = pair_elem(acc[0][i / 2], i & 1);
+                const float nxt = __shfl_down_sync(0xffffffffu, v, 1);
+                if (ok && tok0 + i < M && (r & 1) == 0)
+                  multimem_add_bf16x2(C + static_cast<size_t>(tok0 + i) * p.ldc, pack_bf16x2(v, nxt));
+              }
+              fence_acq_rel_sys();
+            } else if (ok) {
               if (p.out_f32) {
                 float* C = static_cast<float*>(p.out) + col;
 #pragma unroll

@@ -45,6 +45,7 @@ struct GemmParams {
   float* ws;         // decode split-K partials
   int* cnt;          // decode split-K arrival counters, one per tile, zero between launches
   int* status;       // library status word
+  int out_mc;        // plain bf16: `out` is a multicast address; tiles are added into every rank's copy
 };
 
 template <bool FUSED, bool PAIR = false>
@@ -373,11 +374,17 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
                                                   static_cast<size_t>(row) * p.ldc + static_cast<size_t>(nb) * 128);
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              dst[j] = make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
-                                  pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
-                                  pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
-                                  pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
+            for (int j = 0; j < 16; ++j) {
+              const uint4 v = make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
+                                         pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
+                                         pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
+                                         pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
+              if (p.out_mc)
+                multimem_add_bf16x8(dst + j, v);  // tensor-parallel partial: summed into every rank's output
+              else
+                dst[j] = v;
+            }
+            if (p.out_mc) fence_acq_rel_sys();
           }
         }
       } else {

@@ -30,6 +30,7 @@ SIGNATURES = {
     "bs_fp8_gemm_silu_quant": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "bs_fp8_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "bs_fp8_gemm_noalloc": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP]),
+    "bs_fp8_gemm_reduce_multicast": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "bs_fp8_group_quant": (_I, [_VP, _I, _VP, _VP, _I, _I, _VP]),
     "bs_fp8_rmsnorm_group_quant": (_I, [_VP, _I, _VP, _I, _VP, ctypes.c_float, _VP, _VP, _I, _I, _VP]),
     "bs_fp8_pack_tiles": (_I, [_VP, _VP, _I, _I, _VP]),

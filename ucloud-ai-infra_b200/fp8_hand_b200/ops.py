@@ -144,6 +144,29 @@ def gemm(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, *
     return out
 
 
+def gemm_reduce_multicast(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, out: torch.Tensor,
+                          out_multicast: int, *, b_tiled: bool = False) -> torch.Tensor:
+    """Row-parallel GEMM fused with the tensor-parallel sum: this rank's bf16 product is added into every
+    rank's copy of `out` through the NVSwitch multicast address `out_multicast` (the address of out[0, 0] in
+    the group's multicast mapping). `out` is this rank's copy, bf16 [M, N]; every rank zeroes its copy and
+    the group synchronises before the call, and again before `out` is read."""
+    dev, A2, As2, Bs2, M, N, K = _check_operands(A, B, As, Bs, b_tiled)
+    _need(out.dtype == torch.bfloat16, "output must be bf16 (the switch adds bf16 pairs)")
+    _need(out.device == dev and out.dim() == 2 and tuple(out.shape) == (M, N), "output must be [M, N]")
+    _need(out.stride(-1) == 1, "output rows must be contiguous")
+    _need(isinstance(out_multicast, int) and out_multicast != 0, "a multicast address is required")
+    ldc = out.stride(0) if M > 1 else N
+    lib = _native.lib()
+    with _native.device_guard(dev):
+        ws_bytes = lib.bs_fp8_workspace_bytes(M, N, K, 0)
+        ws = _native.workspace(dev, ws_bytes)
+        _native.check(lib.bs_fp8_gemm_reduce_multicast(
+            A2.data_ptr(), _as_bytes(B).data_ptr(), out_multicast, As2.data_ptr(), Bs2.data_ptr(), M, N, K, ldc,
+            int(b_tiled), _native.ptr(ws), 0 if ws is None else ws.numel(), _native.stream_handle(dev)),
+            "bs_fp8_gemm_reduce_multicast")
+    return out
+
+
 def gemm_silu_quant(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, *,
                     b_tiled: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """gate_up GEMM + SiLU(gate)*up + per-token-group quant: B holds [gate; up] (2I rows).

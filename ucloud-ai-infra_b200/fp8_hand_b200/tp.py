@@ -15,6 +15,11 @@ B200-side extension the north star asks for:
            processed in chunks and each chunk's all_reduce runs asynchronously while the next chunk
            computes; the library's persistent kernels then leave SMs free for NCCL when
            BS_FP8_SM_LIMIT caps their grid.
+           reduce="multimem": no separate collective. The output is a symmetric-memory buffer with an
+           NVSwitch multicast mapping, and the down_proj kernel adds each finished bf16 tile into every
+           rank's copy (bs_fp8_gemm_reduce_multicast), so the reduction overlaps the GEMM tile by tile.
+           A one-element NCCL all_reduce orders the zeroing of the copies before the GEMMs and the GEMMs
+           before the result is read.
 
 The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
 the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
@@ -82,15 +87,41 @@ class TensorParallelMLP:
     """x [M, H] bf16 (replicated) -> quant -> fused gate_up_r -> down_r -> all_reduce -> [M, H]."""
 
     def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.bfloat16, compute=None,
-                 chunks: int = 1):
+                 chunks: int = 1, reduce: str = "nccl"):
         if compute is None:
             from . import ops as compute
+        if reduce not in ("nccl", "multimem"):
+            raise ValueError(f"reduce must be 'nccl' or 'multimem', not {reduce!r}")
+        if reduce == "multimem" and partial_dtype != torch.bfloat16:
+            raise ValueError("the multicast reduction adds bf16 partials")
         self.shard = shard
         self.group = group
         self.partial_dtype = partial_dtype
         self.compute = compute
         self.chunks = max(1, int(chunks))
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.reduce = reduce if self.world > 1 else "nccl"
+        self._mc: dict[int, tuple] = {}  # rows -> (this rank's output copy, symmetric-memory handle, mc address)
+        self._flag = None
+
+    def _sync(self, device) -> None:
+        """Orders every rank's earlier kernels on its stream before every rank's later ones."""
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def multicast_out(self, m: int, n: int, device) -> tuple:
+        """This rank's copy of the [m, n] bf16 output in symmetric memory and its multicast address
+        (collective: every rank calls it with the same m on its first use)."""
+        if m not in self._mc:
+            import torch.distributed._symmetric_memory as symm_mem
+            out = symm_mem.empty(m, n, dtype=torch.bfloat16, device=device)
+            handle = symm_mem.rendezvous(out, self.group if self.group is not None else dist.group.WORLD)
+            base = handle.multicast_ptr
+            if not base:
+                raise RuntimeError("the group has no NVSwitch multicast mapping (NVLS)")
+            self._mc[m] = (out, handle, base + (out.data_ptr() - handle.buffer_ptrs[handle.rank]))
+        return self._mc[m]
 
     def partial(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's [M, H] contribution (before the reduction)."""
@@ -105,6 +136,18 @@ class TensorParallelMLP:
         return [(r, min(r + step, m)) for r in range(0, m, step)]
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.reduce == "multimem":
+            # The returned tensor is this rank's copy of the buffer: the next call with the same row count
+            # overwrites it.
+            c, s = self.compute, self.shard
+            out, _, mc = self.multicast_out(x.shape[0], s.down.shape[0] * (BLOCK if s.tiled else 1), x.device)
+            out.zero_()
+            self._sync(x.device)
+            A, As = c.group_quant(x)
+            Q, Qs = c.gemm_silu_quant(A, s.gate_up, As, s.gate_up_scale, b_tiled=s.tiled)
+            c.gemm_reduce_multicast(Q, s.down, Qs, s.down_scale, out, mc, b_tiled=s.tiled)
+            self._sync(x.device)
+            return out
         if self.world == 1 or self.chunks == 1 or x.shape[0] <= BLOCK:
             part = self.partial(x)
             if self.world > 1:
