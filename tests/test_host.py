@@ -70,6 +70,12 @@ def test_argument_validation_needs_no_gpu(lib):
     assert lib.bs_fp8_rmsnorm_group_quant(None, 17408, None, 17408, None, 1e-6, None, None, 4, 17408, s) == 1
     # null pointers with a real shape
     assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
+    # the multicast-reduction GEMM: the same shape rules (bf16 output only), M == 0 a no-op
+    assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 0, 256, 256, 256, 0, None, 0, s) == 0
+    assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 4, 256, 200, 256, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 4, 256, 256, 128, 0, None, 0, s) == 1
+    assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 4, 256, 256, 256, 3, None, 0, s) == 1
+    assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 4, 256, 256, 256, 0, None, 0, s) == 1
 
 
 def _decode_grid(sms, tiles, kb):
