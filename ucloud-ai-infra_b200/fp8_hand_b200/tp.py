@@ -19,7 +19,7 @@ B200-side extension the north star asks for:
            NVSwitch multicast mapping, and the down_proj kernel adds each finished bf16 tile into every
            rank's copy (bs_fp8_gemm_reduce_multicast), so the reduction overlaps the GEMM tile by tile.
            A one-element NCCL all_reduce orders the zeroing of the copies before the GEMMs and the GEMMs
-           before the result is read.
+           before the result is read. `chunks` does not apply: the reduction already overlaps the GEMM.
 
 The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
 the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
