@@ -8,7 +8,8 @@ fused gate_up (K=5120, N2=2x17408) + SiLU*up + per-token-group quant -> down_pro
 weights; the SGLang call sites are stood in by fp8_hand_b200.sglang_compat). With N > 1 the same
 MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel into
 bf16 partials summed by one NCCL all_reduce (optionally in row chunks overlapped with compute,
---tp-chunks); total work is fixed, so scaling is "strong".
+--tp-chunks) or, with --tp-reduce multimem, added by the down_proj epilogue into every rank's output
+through NVSwitch multicast; total work is fixed, so scaling is "strong".
 
 Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e`
 repeats the step with the input copied from pinned host memory and the output copied back inside
@@ -245,11 +246,18 @@ def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="multimem"):
     del gu_q, dn_q
     mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce)
     if tp_reduce == "multimem":
+        # Set up the multicast output (collective), then agree on the outcome: if any rank could not map it,
+        # every rank uses the NCCL all_reduce, so no rank waits in a collective the others skip.
+        ok, why = 1, ""
         try:
-            mlp.multicast_out(M_PREFILL, HIDDEN, device)  # collective; every rank sees the same outcome
-        except RuntimeError as e:
-            if rank == 0:
-                print(f"bench: multicast reduction unavailable ({e}); using the NCCL all_reduce", file=sys.stderr)
+            mlp.multicast_out(M_PREFILL, HIDDEN, device)
+        except Exception as e:  # noqa: BLE001 - any failure to map the buffer selects NCCL on every rank
+            ok, why = 0, f"{type(e).__name__}: {e}"
+        flag = torch.tensor([ok], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if not flag.item():
+            print(f"bench rank {rank}: multicast reduction unavailable ({why or 'on another rank'}); "
+                  "using the NCCL all_reduce", file=sys.stderr)
             mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks)
     return (mlp, (shard.gate_up, shard.gate_up_scale), (shard.down, shard.down_scale), 2 * INTER // world)
 
