@@ -6,10 +6,11 @@ One step = one MLP of BASELINE config 3 at M = 8192 tokens: activation group qua
 fused gate_up (K=5120, N2=2x17408) + SiLU*up + per-token-group quant -> down_proj
 (K=17408, N=5120) -> bf16 [8192, 5120], through the drop-in API (GatedMLP with relayouted
 weights; the SGLang call sites are stood in by fp8_hand_b200.sglang_compat). With N > 1 the same
-MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel into
-bf16 partials summed by one NCCL all_reduce (optionally in row chunks overlapped with compute,
---tp-chunks) or, with --tp-reduce multimem, added by the down_proj epilogue into every rank's output
-through NVSwitch multicast; total work is fixed, so scaling is "strong".
+MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel, its bf16
+partials added by the down_proj epilogue into every rank's output through NVSwitch multicast (the
+default, --tp-reduce multimem; every rank falls back to NCCL if any rank cannot map the multicast
+buffer) or summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped with
+compute, --tp-chunks); total work is fixed, so scaling is "strong".
 
 Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e`
 repeats the step with the input copied from pinned host memory and the output copied back inside
@@ -539,7 +540,7 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--tp-chunks", type=int, default=TP_CHUNKS,
                     help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
-    ap.add_argument("--tp-reduce", choices=("multimem", "nccl"), default="nccl",
+    ap.add_argument("--tp-reduce", choices=("multimem", "nccl"), default="multimem",
                     help="N > 1: sum the down_proj partials in its epilogue through NVSwitch multicast "
                          "(falls back to NCCL where the group has no multicast mapping) or with NCCL")
     ap.add_argument("--ref-rows", type=int, default=512)

@@ -56,7 +56,8 @@ struct PrefillCfg {
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = (PAIR ? 128 : 256) * 128;  // a pair CTA holds half of the weight rows
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 + 128 * 2 * 4 : 0;  // half groups + amax halves
+  // fused: half groups + amax halves; plain: a 4 KB row-transpose buffer per promotion warp (multicast output)
+  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 + 128 * 2 * 4 : 8 * 4096;
   static constexpr int kBarOff = kStages * kStageBytes + kXchBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers, then slack for 1 KB alignment
   static constexpr int kTmemCols = 512;
@@ -363,7 +364,39 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
 
       BS_TR_MARK();
       if constexpr (!FUSED) {
-        if (ok && row_ok && col_ok) {
+        if (p.out_mc) {
+          // Tensor-parallel partial added into every rank's output through the switch. Row-contiguous
+          // runs travel best, so each warp transposes its 32 rows x 64 columns through a 4 KB buffer:
+          // a thread writes its row's eight 16-byte chunks (XOR-swizzled by row), then each instruction
+          // adds 4 rows x 128 contiguous bytes. col_ok is uniform per warp; every lane takes part.
+          if (col_ok) {
+            uint4* buf = reinterpret_cast<uint4*>(xch) + warp * 256;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int j = 8 * h + c;  // columns 8j .. 8j+7 of this thread's 128
+                buf[lane * 8 + (c ^ (lane & 7))] =
+                    make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
+                               pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
+                               pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
+                               pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
+              }
+              __syncwarp();
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int rr = 4 * i + (lane >> 3), cc = lane & 7;
+                const int grow = tm * Cfg::kRows + row0 + q * 32 + rr;
+                const uint4 v = buf[rr * 8 + (cc ^ (rr & 7))];
+                if (ok && grow < M)
+                  multimem_add_bf16x8(static_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(grow) * p.ldc +
+                                          static_cast<size_t>(nb) * 128 + h * 64 + cc * 8,
+                                      v);
+              }
+              __syncwarp();
+            }
+          }
+        } else if (ok && row_ok && col_ok) {
           if (p.out_f32) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(row) * p.ldc +
                                                     static_cast<size_t>(nb) * 128);
@@ -374,17 +407,11 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
                                                   static_cast<size_t>(row) * p.ldc + static_cast<size_t>(nb) * 128);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint4 v = make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
-                                         pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
-                                         pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
-                                         pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
-              if (p.out_mc)
-                multimem_add_bf16x8(dst + j, v);  // tensor-parallel partial: summed into every rank's output
-              else
-                dst[j] = v;
-            }
-            if (p.out_mc) fence_acq_rel_sys();
+            for (int j = 0; j < 16; ++j)
+              dst[j] = make_uint4(pack_bf16x2(lo_f(acc[4 * j]), hi_f(acc[4 * j])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 1]), hi_f(acc[4 * j + 1])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 2]), hi_f(acc[4 * j + 2])),
+                                  pack_bf16x2(lo_f(acc[4 * j + 3]), hi_f(acc[4 * j + 3])));
           }
         }
       } else {
@@ -462,6 +489,9 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
   }
 
   // ------------------------------------------------------------ teardown
+  // Multicast output: this thread's additions through the switch are complete before the kernel ends.
+  if constexpr (!FUSED)
+    if (p.out_mc && warp < 8) fence_acq_rel_sys();
   tc_fence_before();
   __syncthreads();
   // Pair: neither CTA leaves while the leader's MMAs (drained above) or the peer's remote
