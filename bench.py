@@ -7,10 +7,12 @@ fused gate_up (K=5120, N2=2x17408) + SiLU*up + per-token-group quant -> down_pro
 (K=17408, N=5120) -> bf16 [8192, 5120], through the drop-in API (GatedMLP with relayouted
 weights; the SGLang call sites are stood in by fp8_hand_b200.sglang_compat). With N > 1 the same
 MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel, its bf16
-partials added by the down_proj epilogue into every rank's output through NVSwitch multicast (the
-default, --tp-reduce multimem; every rank falls back to NCCL if any rank cannot map the multicast
-buffer) or summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped with
-compute, --tp-chunks); total work is fixed, so scaling is "strong".
+partials either added by the down_proj epilogue into every rank's output through NVSwitch multicast
+(--tp-reduce multimem; every rank falls back to NCCL if any rank cannot map the multicast buffer) or
+summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped with compute,
+--tp-chunks). The default, auto, takes the multicast path on 2 GPUs and NCCL from 4, as measured: each
+rank's additions land in every rank's copy, so a GPU takes in N x the partial bytes, against about twice
+them for a ring all_reduce. Total work is fixed, so scaling is "strong".
 
 Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e`
 repeats the step with the input copied from pinned host memory and the output copied back inside
@@ -234,7 +236,7 @@ def fp8_peak_tflops(device) -> float:
 
 
 # ----------------------------------------------------------------------------- our arm
-def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="multimem"):
+def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="auto"):
     from fp8_hand_b200 import fp8_hand_sm100, sglang_compat, tp
     gu_q, gu_s, dn_q, dn_s = make_weights(device)
     if world == 1:
@@ -245,6 +247,8 @@ def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="multimem"):
         return (mlp, (mlp.gate_up_proj.weight.tiles, gu_s), (mlp.down_proj.weight.tiles, dn_s), 2 * INTER)
     shard = tp.make_shard(gu_q, gu_s, dn_q, dn_s, rank, world, device=device, tiled=True)
     del gu_q, dn_q
+    if tp_reduce == "auto":
+        tp_reduce = "multimem" if world == 2 else "nccl"
     mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce)
     if tp_reduce == "multimem":
         # Set up the multicast output (collective), then agree on the outcome: if any rank could not map it,
@@ -540,9 +544,10 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--tp-chunks", type=int, default=TP_CHUNKS,
                     help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
-    ap.add_argument("--tp-reduce", choices=("multimem", "nccl"), default="multimem",
+    ap.add_argument("--tp-reduce", choices=("auto", "multimem", "nccl"), default="auto",
                     help="N > 1: sum the down_proj partials in its epilogue through NVSwitch multicast "
-                         "(falls back to NCCL where the group has no multicast mapping) or with NCCL")
+                         "(falls back to NCCL where the group has no multicast mapping) or with NCCL; "
+                         "auto: multicast on 2 GPUs, NCCL from 4 (measured faster there)")
     ap.add_argument("--ref-rows", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
