@@ -1,26 +1,30 @@
 """Benchmark of the block-FP8 MLP hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --kernel fused|gemm|quant|norm --M 2048 [--N 34816] [--K 5120] [--iters 2] [--warmup 1]
 
-One step = one MLP of BASELINE config 3 at M = 8192 tokens: activation group quant ->
-fused gate_up (K=5120, N2=2x17408) + SiLU*up + per-token-group quant -> down_proj
-(K=17408, N=5120) -> bf16 [8192, 5120], through the drop-in API (GatedMLP with relayouted
-weights; the SGLang call sites are stood in by fp8_hand_b200.sglang_compat). With N > 1 the same
-MLP runs tensor-parallel: gate_up column-parallel, down_proj row-parallel, its bf16
-partials either added by the down_proj epilogue into every rank's output through NVSwitch multicast
-(--tp-reduce multimem; every rank falls back to NCCL if any rank cannot map the multicast buffer) or
-summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped with compute,
---tp-chunks). The default, auto, takes the multicast path on 2 GPUs and NCCL from 4, as measured: each
-rank's additions land in every rank's copy, so a GPU takes in N x the partial bytes, against about twice
-them for a ring all_reduce. Total work is fixed, so scaling is "strong".
+One step = the prefill MLP at M = 8192 tokens (K = 5120, I = 17408): activation group quant -> fused
+gate_up (N2 = 2 x 17408) + SiLU*up + per-token-group quant -> down_proj (K = 17408, N = 5120) -> bf16
+[8192, 5120], through the drop-in API (GatedMLP with relayouted weights; the SGLang call sites are stood in by
+fp8_hand_b200.sglang_compat). With N > 1 the same MLP runs tensor-parallel: gate_up column-parallel, down_proj
+row-parallel, its bf16 partials either added by the down_proj epilogue into every rank's output through
+NVSwitch multicast (--tp-reduce multimem, two ranks only; every rank falls back to NCCL if any rank cannot map
+the multicast buffer) or summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped
+with compute, --tp-chunks). The default, auto, takes the multicast path on 2 GPUs and NCCL from 4. Total work is
+fixed, so scaling is "strong".
 
-Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e`
-repeats the step with the input copied from pinned host memory and the output copied back inside
-the timed region. Timing: CUDA events on the launching stream, barrier + synchronize around the
-timed region, max over ranks. Weights (267 MB) and x (84 MB) are larger than the 126 MB L2.
+Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e` repeats the step
+with the input copied from pinned host memory and the output copied back inside the timed region. Timing:
+CUDA events on the launching stream, barrier + synchronize around the timed region, max over ranks. Weights
+(267 MB) and x (84 MB) are larger than the 126 MB L2. The other keys cover the remaining configured workloads:
+the MLP at M = 1024 and 4096, decode sizes M <= 112 (HBM GB/s), the single GEMM M = 128 x 6144 x 5120, the
+decoder layer's other linears, the fused RMSNorm + quant and the vocab-sized lm_head.
 
---impl reference times the reference's own CPU path (its torch dequantise-then-matmul oracle,
-restated in oracle/) on the host cores for a bounded row sample of the same workload.
+--impl reference times the reference's own CPU path (its torch dequantise-then-matmul oracle, restated in
+oracle/) on the host cores, on the same 8192-token workload.
+
+--kernel runs one kernel case alone (after its warm-up, nothing else launches), the command the ncu captures
+under profiles/ were taken on.
 """
 from __future__ import annotations
 
@@ -47,12 +51,15 @@ M_PREFILL = 8192
 HIDDEN = 5120
 INTER = 17408
 DECODE_MS = (1, 8, 14, 56, 112)
+PREFILL_MS = (1024, 4096)
+L2_BYTES = 126 * 2 ** 20
 # Tensor parallel (N > 1): rows per MLP step split into TP_CHUNKS chunks whose all_reduce overlaps the next
 # chunk's GEMMs; the GEMM kernels' persistent grids use TP_SM_LIMIT SMs, NCCL at most TP_NCCL_CTAS CTAs.
 TP_CHUNKS = 1
 TP_NCCL_CTAS = 16
 TP_SM_LIMIT = 148 - TP_NCCL_CTAS
-# RTX 4090 hand kernels: fused gate_up 9.25 ms + down_proj 4.595 ms at M = 8192.
+# The reference's published RTX 4090 hand kernels: fused gate_up 9.25 ms + down_proj 4.595 ms at M = 8192
+# (docs/OPTIMIZATION_REPORT.md:160, :173-177).
 REF_4090_MLP_MS = 9.25 + 4.595
 FP8_NOMINAL_TFLOPS = 4500.0
 
@@ -64,6 +71,11 @@ def mlp_flops(M: int) -> float:
 def fused_bytes(M: int, N2: int = 2 * INTER, K: int = HIDDEN) -> float:
     """Algorithmic bytes of one fused gate_up call."""
     return M * K + N2 * K + 4 * M * K / 128 + 4 * (N2 / 128) * (K / 128) + M * N2 / 2 + 4 * M * N2 / 256
+
+
+def gemm_bytes(M: int, N: int, K: int) -> float:
+    """Algorithmic bytes of one bf16-output GEMM call."""
+    return N * K + M * K + 4 * M * K / 128 + 4 * (N / 128) * (K / 128) + 2 * M * N
 
 
 def measured_peaks() -> dict:
@@ -133,14 +145,22 @@ def block_quant_cuda(w: torch.Tensor, rows: int):
     return q, s.float().contiguous()
 
 
-def make_weights(device, seed=0):
+def make_weight(n, k, device, seed, chunk=32768):
+    """bf16 N(0, 0.02) [n, k] block-quantised 128 x 128, made on the GPU in row chunks."""
     g = torch.Generator(device=device).manual_seed(seed)
-    gu = torch.randn(2 * INTER, HIDDEN, device=device, generator=g, dtype=torch.float32) * 0.02
-    gu_q, gu_s = block_quant_cuda(gu.to(torch.bfloat16).float(), 128)
-    del gu
-    dn = torch.randn(HIDDEN, INTER, device=device, generator=g, dtype=torch.float32) * 0.02
-    dn_q, dn_s = block_quant_cuda(dn.to(torch.bfloat16).float(), 128)
-    del dn
+    q = torch.empty(n, k, dtype=torch.float8_e4m3fn, device=device)
+    s = torch.empty(n // 128, k // 128, dtype=torch.float32, device=device)
+    for r0 in range(0, n, chunk):
+        r1 = min(n, r0 + chunk)
+        w = (torch.randn(r1 - r0, k, device=device, generator=g) * 0.02).to(torch.bfloat16).float()
+        q[r0:r1], s[r0 // 128:r1 // 128] = block_quant_cuda(w, 128)
+        del w
+    return q, s
+
+
+def make_weights(device, seed=0):
+    gu_q, gu_s = make_weight(2 * INTER, HIDDEN, device, seed)
+    dn_q, dn_s = make_weight(HIDDEN, INTER, device, seed + 1)
     return gu_q, gu_s, dn_q, dn_s
 
 
@@ -152,6 +172,12 @@ def make_x(M, device, seed=1, outlier_frac=0.01):
         rows = torch.randperm(M, device=device, generator=g)[:n]
         x[rows] *= 50.0
     return x.to(torch.bfloat16)
+
+
+def make_acts(M, K, device, seed):
+    from fp8_hand_b200 import ops
+    g = torch.Generator(device=device).manual_seed(seed)
+    return ops.group_quant(torch.randn(M, K, device=device, generator=g).to(torch.bfloat16))
 
 
 # ----------------------------------------------------------------------------- timing helpers
@@ -168,49 +194,110 @@ def max_over_ranks(v: float, world: int, device) -> float:
     return t.item()
 
 
+def event_ms(fn, warmup=3, reps=5) -> float:
+    """Median of `reps` event-timed calls on the current stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def make_graph_timer(device, world, reps=50):
+    """Per-call microseconds of fn (or of fns, cycled) as a CUDA graph of `reps` back-to-back calls: a decode
+    step is served from a captured graph, and the Python wrapper costs more than the kernel. Passing several
+    closures over different weight copies rotates a working set larger than L2 through the graph."""
+    stream = torch.cuda.current_stream(device)
+
+    def graph_us(fn):
+        fns = fn if isinstance(fn, (list, tuple)) else [fn]
+        side = torch.cuda.Stream(device)
+        with torch.cuda.stream(side):
+            for _ in range(3):  # also sizes this stream's decode workspace before capture
+                for f in fns:
+                    f()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(reps):
+                fns[i % len(fns)]()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        g.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return max_over_ranks(s.elapsed_time(e) / reps, world, device) * 1e3
+
+    return graph_us
+
+
+def copies_over_l2(nbytes: int) -> int:
+    """Weight copies whose total exceeds L2, so rotating through them streams from HBM."""
+    return max(1, -(-(L2_BYTES + 1) // nbytes))
+
+
 def linear_set(device, hbm, graph_us) -> dict:
-    """the other block-FP8 linears of a layer at M=8192 (TFLOP/s, event-timed median of
-    5 launches), the fused RMSNorm + activation quant, and the vocab-sized lm_head at decode sizes (GB/s,
-    CUDA graph), random-init weights."""
-    from fp8_hand_b200 import kernel_bench as kbench, ops
+    """The remaining configured single-GPU workloads: the single GEMM M = 128 x N 6144 x K 5120 (GB/s), the
+    decoder layer's other linears at M = 8192 (TFLOP/s, event-timed median of 5 launches), the fused RMSNorm
+    + activation quant, and the vocab-sized lm_head at decode sizes in the layouts the drop-in path gives it
+    (row-major: relayout leaves lm_head alone) and tile-first, CUDA-graph timed, random-init weights."""
+    from fp8_hand_b200 import ops
     out = {}
+    # single GEMM (config 1): the 31.5 MB weight fits in L2, so the graph rotates through enough copies
+    m, n, k = 128, 6144, 5120
+    copies = [make_weight(n, k, device, seed=20 + i) for i in range(copies_over_l2(n * k))]
+    tiled = [(ops.pack_tiles(q), s) for q, s in copies]
+    A, As = make_acts(m, k, device, seed=21)
+    C = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+    for name, ws, bt in (("tiled", tiled, True), ("row_major", copies, False)):
+        us = graph_us([lambda w=w, s=s: ops.gemm(A, w, As, s, b_tiled=bt, out=C) for w, s in ws])
+        gbs = gemm_bytes(m, n, k) / (us * 1e-6) / 1e9
+        out[f"gemm_m{m}_k{k}_n{n}_{name}"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                                              "frac_hbm": round(gbs / hbm, 3), "weight_copies": len(ws)}
+    del copies, tiled
     for name, n, k in (("qkv", 10240, 5120), ("o", 5120, 6144)):
-        tiles, s = kbench._weights(n, k, device)
-        A, As = kbench._acts(M_PREFILL, k, device)
+        q, s = make_weight(n, k, device, seed=n + k)
+        tiles = ops.pack_tiles(q)
+        A, As = make_acts(M_PREFILL, k, device, seed=n)
         C = torch.empty(M_PREFILL, n, dtype=torch.bfloat16, device=device)
-        for _ in range(3):
-            ops.gemm(A, tiles, As, s, b_tiled=True, out=C)
-        times = []
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            ops.gemm(A, tiles, As, s, b_tiled=True, out=C)
-            e1.record()
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        ms = statistics.median(times)
+        ms = event_ms(lambda: ops.gemm(A, tiles, As, s, b_tiled=True, out=C))
         out[f"{name}_m{M_PREFILL}_k{k}_n{n}"] = {"ms": round(ms, 4),
                                                  "TFLOP/s": round(2.0 * M_PREFILL * n * k / (ms * 1e-3) / 1e12, 1)}
-        del tiles, s, A, As, C
-    # RMSNorm fused with the activation quant (SURVEY 8f.1), with and without the fused residual add
+        del q, s, tiles, A, As, C
+    # RMSNorm fused with the activation quant, with and without the fused residual add
     k = HIDDEN
     w = torch.ones(k, dtype=torch.bfloat16, device=device)
-    for m, add in ((M_PREFILL, False), (M_PREFILL, True), (112, True)):
+    for m, add in ((M_PREFILL, False), (M_PREFILL, True), (112, True), (112, False)):
         xm = make_x(m, device, seed=4, outlier_frac=0.0)
         res = make_x(m, device, seed=5, outlier_frac=0.0) if add else None
         us = graph_us(lambda: ops.rmsnorm_group_quant(xm, w, 1e-6, residual=res))
         nbytes = m * k * (2 + 1 + 4 / 128) + (4 * m * k if add else 0) + 2 * k
         out[f"rmsnorm_quant_m{m}_k{k}" + ("_add" if add else "")] = {
-            "us": round(us, 2), "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1), "frac_hbm": round(nbytes / (us * 1e-6) / 1e9 / hbm, 3)}
+            "us": round(us, 2), "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "frac_hbm": round(nbytes / (us * 1e-6) / 1e9 / hbm, 3)}
     n, k = 248320, 5120
-    tiles, s = kbench._weights(n, k, device)
-    for m in (1, 112):
-        A, As = kbench._acts(m, k, device)
-        C = torch.empty(m, n, dtype=torch.bfloat16, device=device)
-        us = graph_us(lambda: ops.gemm(A, tiles, As, s, b_tiled=True, out=C))
-        gbs = (n * k + m * k * (1 + 4 / 128) + 4 * (n // 128) * (k // 128) + 2 * m * n) / (us * 1e-6) / 1e9
-        out[f"lm_head_m{m}_k{k}_n{n}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
-    del tiles, s
+    q, s = make_weight(n, k, device, seed=7)
+    layouts = (("row_major", q, False), ("tiled", ops.pack_tiles(q), True))
+    for lname, wt, bt in layouts:
+        for m in (1, 112):
+            A, As = make_acts(m, k, device, seed=8 + m)
+            C = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+            us = graph_us(lambda: ops.gemm(A, wt, As, s, b_tiled=bt, out=C))
+            gbs = gemm_bytes(m, n, k) / (us * 1e-6) / 1e9
+            out[f"lm_head_m{m}_k{k}_n{n}_{lname}"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                                                      "frac_hbm": round(gbs / hbm, 3)}
+    del q, s, layouts
     torch.cuda.empty_cache()
     return out
 
@@ -247,9 +334,9 @@ def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="auto"):
         return (mlp, (mlp.gate_up_proj.weight.tiles, gu_s), (mlp.down_proj.weight.tiles, dn_s), 2 * INTER)
     shard = tp.make_shard(gu_q, gu_s, dn_q, dn_s, rank, world, device=device, tiled=True)
     del gu_q, dn_q
-    if tp_reduce == "auto":
+    if tp_reduce == "auto" or (tp_reduce == "multimem" and world > 2):
         tp_reduce = "multimem" if world == 2 else "nccl"
-    mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce)
+    mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce, return_buffer=True)
     if tp_reduce == "multimem":
         # Set up the multicast output (collective), then agree on the outcome: if any rank could not map it,
         # every rank uses the NCCL all_reduce, so no rank waits in a collective the others skip.
@@ -313,6 +400,10 @@ def run_ours(args, rank, world, device) -> dict | None:
     fused_ms = max_over_ranks(fused_ms, world, device)
     tflops = mlp_flops(M_PREFILL) / (ms * 1e-3) / 1e12
     assert torch.isfinite(out.float()).all().item(), "non-finite MLP output"
+    out_sample = None
+    if world == 1:
+        # kept for the CPU-baseline leg's parity check of sampled rows (outside every timed region)
+        out_sample = out.clone()
 
     # e2e: every step copies its input from pinned host memory to the device, runs the MLP through
     # the public API and copies the result back to pinned host memory, all inside the timed region.
@@ -359,37 +450,35 @@ def run_ours(args, rank, world, device) -> dict | None:
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
     clk.__exit__(None, None, None)
+    del xd, od
 
-    # Decode / verify sizes on this rank's shard, HBM GB/s: fused gate_up (config 2) and the
-    # down_proj GEMM. A decode step is served from a captured CUDA graph, so each size is timed as a
-    # graph of `reps` back-to-back calls (host launch overhead excluded), max over ranks.
+    # The MLP at the other prefill sizes (same weights, event-timed median of 5 steps, max over ranks).
+    prefill = {}
+    for M in PREFILL_MS:
+        xm = make_x(M, device, seed=3)
+        fused_events.clear()
+        ops.gemm_silu_quant = timed_fused
+        try:
+            mms = event_ms(lambda: step(xm))
+        finally:
+            ops.gemm_silu_quant = orig_fused
+        mms = max_over_ranks(mms, world, device)
+        fms = max_over_ranks(statistics.median(s.elapsed_time(e) for s, e in fused_events), world, device)
+        prefill[str(M)] = {"ms": round(mms, 4), "TFLOP/s": round(mlp_flops(M) / (mms * 1e-3) / 1e12, 1),
+                           "fused_ms": round(fms, 4),
+                           "fused_TFLOP/s": round(2.0 * M * n2_local * HIDDEN / (fms * 1e-3) / 1e12, 1)}
+
+    # Decode / verify sizes on this rank's shard, HBM GB/s: fused gate_up and the down_proj GEMM, each timed
+    # as a CUDA graph of back-to-back calls, max over ranks. down_proj's 89 MB weight (per rank: 1/N of it)
+    # fits in L2, so its graph rotates through enough weight copies to stream from HBM.
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
-    reps = 50
-
-    def graph_us(fn):
-        side = torch.cuda.Stream(device)
-        with torch.cuda.stream(side):
-            for _ in range(3):  # also sizes this stream's decode workspace before capture
-                fn()
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=side):
-            for _ in range(reps):
-                fn()
-        g.replay()
-        torch.cuda.synchronize()
-        barrier(world)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        g.replay()
-        e.record(stream)
-        torch.cuda.synchronize()
-        del g
-        return max_over_ranks(s.elapsed_time(e) / reps, world, device) * 1e3
-
+    graph_us = make_graph_timer(device, world)
     decode, decode_down = {}, {}
     n_down = dn_tiles.shape[0] * 128
+    k_down = dn_tiles.shape[1] * 128
+    n_copies = copies_over_l2(n_down * k_down)
+    dn_copies = [(dn_tiles, dn_s)] + [(dn_tiles.clone(), dn_s.clone()) for _ in range(n_copies - 1)]
     for M in DECODE_MS:
         xm = make_x(M, device, seed=2, outlier_frac=0.0)
         A, As = ops.group_quant(xm)
@@ -398,10 +487,25 @@ def run_ours(args, rank, world, device) -> dict | None:
         decode[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
         Q, Qs = ops.gemm_silu_quant(A, gu_tiles, As, gu_s, b_tiled=True)
         yd = torch.empty(M, n_down, dtype=torch.bfloat16, device=device)
-        us = graph_us(lambda: ops.gemm(Q, dn_tiles, Qs, dn_s, b_tiled=True, out=yd))
-        k_down = Q.shape[1]
-        gbs = (n_down * k_down + M * k_down * (1 + 4 / 128) + 2 * M * n_down) / (us * 1e-6) / 1e9
+        us = graph_us([lambda w=w, s=s: ops.gemm(Q, w, Qs, s, b_tiled=True, out=yd) for w, s in dn_copies])
+        gbs = gemm_bytes(M, n_down, k_down) / (us * 1e-6) / 1e9
         decode_down[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+    del dn_copies
+
+    # Tensor parallel: the whole MLP at the decode/verify size M = 112 (quant -> fused gate_up -> down_proj ->
+    # reduction), as a CUDA graph of back-to-back steps with the collective inside.
+    tp_decode = None
+    if world > 1:
+        x112 = make_x(112, device, seed=6, outlier_frac=0.0)
+        try:
+            us = graph_us(lambda: mlp(x112))
+            tp_decode = {"M": 112, "us_per_step": round(us, 2),
+                         "TFLOP/s": round(mlp_flops(112) / (us * 1e-6) / 1e12, 2),
+                         "weight_GB/s_per_rank": round((fused_bytes(112, n2_local) +
+                                                        gemm_bytes(112, n_down, k_down)) / (us * 1e-6) / 1e9, 1),
+                         "timing": "CUDA graph of 50 back-to-back MLP steps, collective inside, max over ranks"}
+        except RuntimeError as e:  # every rank runs the same capture, so every rank lands here alike
+            tp_decode = {"M": 112, "unavailable": f"{type(e).__name__}: {e}"[:200]}
 
     fp8_peak = fp8_peak_tflops(device) if rank == 0 else None
     linears = linear_set(device, hbm, graph_us) if world == 1 else None
@@ -415,6 +519,7 @@ def run_ours(args, rank, world, device) -> dict | None:
             key, _, val = line.partition(":")
             if key.strip() == f"fused_prefill_tp{world}" and val.strip():
                 traffic = int(val.strip())
+    reduce_mode = getattr(mlp, "reduce", "nccl")
     res = {
         "metric": METRIC,
         "value": round(tflops, 1),
@@ -433,27 +538,33 @@ def run_ours(args, rank, world, device) -> dict | None:
                         "-> down_proj (K=17408, N=5120), bf16 in/out" +
                         ((f"; config[4] tensor-parallel tp={world}, bf16 partials added into every rank's "
                           "output by the down_proj epilogue through NVSwitch multicast (multimem.red), no "
-                          "separate collective") if getattr(mlp, "reduce", "nccl") == "multimem" else
+                          "separate collective") if reduce_mode == "multimem" else
                          (f"; config[4] tensor-parallel tp={world}, bf16 partials + NCCL all_reduce"
                           + (f" in {args.tp_chunks} row chunks overlapped with compute, GEMM grids on "
                              f"{os.environ.get('BS_FP8_SM_LIMIT', 'all')} SMs" if args.tp_chunks > 1 else ""))
                          if world > 1 else ""),
             "M": M_PREFILL, "hidden": HIDDEN, "intermediate": INTER, "parallelism": f"tp{world}",
-            "l2": "inputs larger than L2 (weights 267 MB + x 84 MB per step vs 126 MB L2)",
+            "l2": "inputs larger than L2 (weights 267 MB + x 84 MB per step vs 126 MB L2); decode weights that fit "
+                  "in L2 are rotated through copies whose total exceeds it",
         },
         "roofline": {
             "kernel": "k_prefill<fused> (gate_up + SiLU*up + quant)",
             "bound": "tensor", "achieved": round(fused_tflops, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
             "frac": round(fused_tflops / fp8_peak, 3),
             "peak_source": "measured: cuBLASLt e4m3 burst, torch._scaled_mm 8192^3 (MEASURED_PEAKS.json has no FP8 figure)",
+            "frac_of_2x_measured_bf16": (round(fused_tflops / (2 * peaks["bf16_tflops"]), 3)
+                                         if "bf16_tflops" in peaks else None),
             "frac_of_nominal_4500": round(fused_tflops / FP8_NOMINAL_TFLOPS, 3),
             "fused_ms": round(fused_ms, 4),
             "traffic": traffic,
         },
+        "prefill_mlp": {"unit": "TFLOP/s", "timing": "event-timed median of 5 steps", "by_M": prefill},
         "decode_fused_gate_up": {"unit": "GB/s", "hbm_peak_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
-                                 "timing": f"CUDA graph of {reps} back-to-back calls", "by_M": decode},
-        "decode_down_proj": {"unit": "GB/s", "hbm_peak_gbs": hbm, "timing": f"CUDA graph of {reps} back-to-back calls",
+                                 "timing": "CUDA graph of 50 back-to-back calls", "by_M": decode},
+        "decode_down_proj": {"unit": "GB/s", "hbm_peak_gbs": hbm,
+                             "timing": f"CUDA graph of 50 back-to-back calls over {n_copies} weight copies",
                              "by_M": decode_down},
+        **({"tp_decode_mlp": tp_decode} if tp_decode else {}),
         "e2e": {"value": round(mlp_flops(M_PREFILL) / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": xh.numel() * xh.element_size(),
@@ -463,7 +574,7 @@ def run_ours(args, rank, world, device) -> dict | None:
         "clocks": clk.summary(),
     }
     if world == 1:
-        res["cpu_baseline"] = cpu_baseline_sample(rows=args.cpu_rows)
+        res["cpu_baseline"] = cpu_baseline_sample(rows=args.cpu_rows, gpu=(x, out_sample, mlp))
     return res
 
 
@@ -495,7 +606,41 @@ class CpuReference:
         return time.perf_counter() - t, mlp_flops(rows)
 
 
-def cpu_baseline_sample(rows: int, reps: int = 3) -> dict:
+def gpu_parity_sample(x, out, mlp, rows=64) -> dict:
+    """Sampled rows of the timed M = 8192 MLP against the oracle, outside every timed region, on rank 0: the
+    fused front half (recomputed for the whole batch, which reproduces the timed step's (Q, Qs) since the MLP is
+    deterministic) against the oracle's restatement of the reference kernel's arithmetic on the same rows, and
+    the output against the oracle's blockwise down_proj of those (Q, Qs) rows, each with its own bar."""
+    from oracle import oracle as O
+    from fp8_hand_b200 import ops
+    g = torch.Generator().manual_seed(17)
+    idx = torch.randperm(M_PREFILL, generator=g)[:rows].sort().values
+    idx_d = idx.to(x.device)
+    gu_t, gu_s = mlp.gate_up_proj.weight.tiles, mlp.gate_up_proj.weight_scale_inv
+    dn_t, dn_s = mlp.down_proj.weight.tiles, mlp.down_proj.weight_scale_inv
+    A, As = ops.group_quant(x)
+    Q, Qs = ops.gemm_silu_quant(A, gu_t, As, gu_s, b_tiled=True)
+    Q_s = Q.view(torch.uint8).index_select(0, idx_d).cpu().view(torch.float8_e4m3fn)
+    Qs_s = Qs.index_select(0, idx_d).cpu()
+
+    def untile(t):  # tile-first bytes [N/128, K/128, 128, 128] -> row-major e4m3 [N, K]
+        nb, kb = t.shape[:2]
+        return t.permute(0, 2, 1, 3).reshape(nb * 128, kb * 128).cpu().view(torch.float8_e4m3fn)
+
+    A_s = A.view(torch.uint8).index_select(0, idx_d).cpu().view(torch.float8_e4m3fn)
+    q_ref, s_ref, _ = O.fused_gate_up(A_s, untile(gu_t), As.index_select(0, idx_d).cpu(), gu_s.cpu())
+    ulp = O.e4m3_ulp_distance(Q_s, q_ref)
+    ref = O.blockwise_matmul(Q_s, untile(dn_t), Qs_s, dn_s.cpu())
+    got = out.index_select(0, idx_d).cpu()
+    return {"rows": rows,
+            "fused": {"scale_max_rel": ((Qs_s - s_ref).abs() / s_ref).max().item(), "q_max_ulp": int(ulp.max()),
+                      "q_frac_differ": round((ulp > 0).float().mean().item(), 7),
+                      "bar": "scales 1e-6 rel; <= 1 e4m3 ulp on <= 0.1% of elements"},
+            "down_proj": {"max_rel": round(O.max_rel_error(got, ref), 6), "norm_rel": round(O.norm_rel_error(got, ref), 6),
+                          "bar": "max rel 1e-2 (floor 1e-3 max|ref|), norm 4e-3"}}
+
+
+def cpu_baseline_sample(rows: int, reps: int = 3, gpu=None) -> dict:
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ref = CpuReference()
@@ -505,9 +650,12 @@ def cpu_baseline_sample(rows: int, reps: int = 3) -> dict:
         s_, f_ = ref.sample(rows, seed=i + 1)
         secs += s_
         flops += f_
-    return {"value": round(flops / secs / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} x {rows} of the {M_PREFILL} tokens of the same MLP (weights dequantised per call "
-                      f"as the reference's ref_matmul does, fp32 matmuls, all host threads), {secs:.1f} s timed"}
+    res = {"value": round(flops / secs / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+           "sample": f"{reps} x {rows} of the {M_PREFILL} tokens of the same MLP (weights dequantised per call "
+                     f"as the reference's ref_matmul does, fp32 matmuls, all host threads), {secs:.1f} s timed"}
+    if gpu is not None:
+        res["gpu_parity_sampled_rows"] = gpu_parity_sample(*gpu)
+    return res
 
 
 def run_reference(args, rank, world) -> dict | None:
@@ -524,15 +672,61 @@ def run_reference(args, rank, world) -> dict | None:
         secs += s_
         flops += f_
     v = round(flops / secs / 1e12, 4)
+    full = args.ref_rows == M_PREFILL
     return {"metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 1), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "impl": "reference",
             "data": "synthetic, same generators as the GPU arm",
-            "config": {"workload": f"config[2] MLP, {args.ref_rows}-token sample of M=8192 per step",
+            "config": {"workload": ("config[2] MLP at M=8192 (every step the whole 8192-token batch)" if full else
+                                    f"config[2] MLP, {args.ref_rows}-token sample of M=8192 per step"),
                        "M": M_PREFILL, "hidden": HIDDEN, "intermediate": INTER, "parallelism": "host cores"},
             "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                              "sample": f"{args.ref_rows} tokens per step of the M=8192 MLP"},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ----------------------------------------------------------------------------- single-kernel cases
+def run_kernel_case(args) -> dict:
+    """One kernel on its own: inputs made first, `warmup` calls, then `iters` timed calls and nothing else
+    (the command the ncu captures under profiles/ run)."""
+    from fp8_hand_b200 import ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    M, N, K = args.M, args.N, args.K
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+    if args.kernel in ("quant", "norm"):
+        g = torch.Generator(device=device).manual_seed(3)
+        x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+        w = torch.ones(K, dtype=torch.bfloat16, device=device)
+        fn = (lambda: ops.group_quant(x)) if args.kernel == "quant" else (lambda: ops.rmsnorm_group_quant(x, w))
+        nbytes = M * K * 3 + M * K / 128 * 4 + (2 * K if args.kernel == "norm" else 0)
+        flops = 0.0
+    else:
+        q, s = make_weight(N, K, device, seed=0)
+        tiles = ops.pack_tiles(q) if args.tiled else q
+        del q
+        A, As = make_acts(M, K, device, seed=1)
+        if args.kernel == "fused":
+            fn = lambda: ops.gemm_silu_quant(A, tiles, As, s, b_tiled=args.tiled)  # noqa: E731
+            nbytes = fused_bytes(M, N, K)
+        else:
+            C = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+            fn = lambda: ops.gemm(A, tiles, As, s, b_tiled=args.tiled, out=C)  # noqa: E731
+            nbytes = gemm_bytes(M, N, K)
+        flops = 2.0 * M * N * K
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.iters
+    return {"kernel": args.kernel, "M": M, "N": N, "K": K, "tiled": bool(args.tiled), "ms": round(ms, 5),
+            "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 1), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 3)}
 
 
 def main() -> int:
@@ -546,10 +740,21 @@ def main() -> int:
                     help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
     ap.add_argument("--tp-reduce", choices=("auto", "multimem", "nccl"), default="auto",
                     help="N > 1: sum the down_proj partials in its epilogue through NVSwitch multicast "
-                         "(falls back to NCCL where the group has no multicast mapping) or with NCCL; "
-                         "auto: multicast on 2 GPUs, NCCL from 4 (measured faster there)")
-    ap.add_argument("--ref-rows", type=int, default=512)
+                         "(two ranks only; falls back to NCCL where the group has no multicast mapping) or with "
+                         "NCCL; auto: multicast on 2 GPUs, NCCL from 4")
+    ap.add_argument("--ref-rows", type=int, default=M_PREFILL,
+                    help="--impl reference: tokens of the M=8192 batch computed per step (default: all)")
+    ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm"), default=None,
+                    help="run one kernel case alone (--M/--N/--K/--iters/--warmup)")
+    ap.add_argument("--M", type=int, default=2048)
+    ap.add_argument("--N", type=int, default=2 * INTER)
+    ap.add_argument("--K", type=int, default=HIDDEN)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--row-major", dest="tiled", action="store_false", help="--kernel: row-major weights")
     args = ap.parse_args()
+    if args.kernel is not None:
+        print(json.dumps(run_kernel_case(args)), flush=True)
+        return 0
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 

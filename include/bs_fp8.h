@@ -51,8 +51,10 @@ extern "C" {
  *   out_dtype  0 = bf16 (the reference's only output), 1 = fp32 (tensor-parallel partials)
  *   ldc        output row stride in elements, >= N, multiple of 8
  * M <= 128 runs the swap-AB split-K decode kernel and needs `workspace` of at least
- * bs_fp8_workspace_bytes(M, N, K, 0) bytes, zero-filled before its first use (the kernel
- * leaves it in that state). M > 128 needs no workspace. M == 0 is a no-op. */
+ * bs_fp8_workspace_bytes(M, N, K, 0) bytes, zero-filled before its first use. Its first 64 KB are
+ * per-tile arrival counters (at most 16384 weight tiles, N <= 2097152), which every call leaves at
+ * zero, so one workspace serves any sequence of shapes on its stream. M > 128 needs no workspace.
+ * M == 0 is a no-op. */
 int bs_fp8_gemm(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
                 int ldc, int b_tiled, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
@@ -92,7 +94,8 @@ int bs_fp8_gemm_reduce_multicast(const void* A, const void* B, void* C_mc, const
 int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N,
                         int K, int ldc, int b_tiled, int out_dtype, void* stream);
 
-/* Workspace bytes the decode kernels need for (M, N, K); 0 when M > 128 or M == 0. */
+/* Workspace bytes the decode kernels need for (M, N, K): the 64 KB counter prefix plus the partial tiles;
+ * 0 when M > 128 or M == 0 (no workspace needed) or when the shape has more than 16384 weight tiles. */
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused);
 
 /* Per-token-group activation quant: x bf16 [M, K] (row stride ldx elements, multiple of 8) ->
@@ -125,6 +128,28 @@ int bs_fp8_status(int* code, int clear);
  * `limit_ns`, leaving BS_ERR_TIMEOUT_SELFTEST in the status word. Exercises the bounded-wait
  * path without any fault. No reference counterpart (the reference has no bounded waits). */
 int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
+/* Launch plan of one GEMM call: what bs_fp8_gemm (fused = 0) or bs_fp8_gemm_silu_quant (fused = 1) launches
+ * for an M x N x K problem on the current device (148 SMs assumed when no device is usable). Fills
+ * plan[0 .. BS_PLAN_FIELDS) (n >= BS_PLAN_FIELDS) with the fields below; returns BS_ERR_ARG for a shape the
+ * GEMMs refuse. Replaces the tile table behind `select(N, M)` (H:51-57, :74-87), which reported the sm_89
+ * kernel variant for a product. */
+#define BS_PLAN_KIND 0        /* 1 decode (swap-AB, M <= 128), 2 prefill                                   */
+#define BS_PLAN_TILE_ROWS 1   /* decode: weight rows per tile (128); prefill: output rows (128, 256 pairs) */
+#define BS_PLAN_TILE_COLS 2   /* decode: tokens padded to a multiple of 16; prefill: output columns (256)  */
+#define BS_PLAN_STAGES 3      /* TMA pipeline stages                                                       */
+#define BS_PLAN_THREADS 4     /* threads per CTA                                                           */
+#define BS_PLAN_GRID 5        /* CTAs launched                                                             */
+#define BS_PLAN_CLUSTER 6     /* CTAs per cluster (2: CTA pairs)                                           */
+#define BS_PLAN_GROUP_M 7     /* prefill raster: M tiles per group (column sweep), 0 when sweeping rows    */
+#define BS_PLAN_GROUP_N 8     /* prefill raster: N tiles per group (row sweep), 0 when sweeping columns    */
+#define BS_PLAN_TMEM_COLS 9   /* TMEM columns allocated per CTA                                            */
+#define BS_PLAN_SPLIT 10      /* decode: 0 one CTA per weight tile, s > 0 equal K splits, -1 stream-K      */
+#define BS_PLAN_WARPGROUPS 11 /* promotion warpgroups                                                      */
+#define BS_PLAN_SMEM 12       /* dynamic shared memory bytes per CTA                                       */
+#define BS_PLAN_TILES 13      /* prefill: output tiles walked by the persistent CTAs                       */
+#define BS_PLAN_FIELDS 14
+int bs_fp8_launch_plan(int M, int N, int K, int fused, int* plan, int n);
 
 /* Number of SMs the kernels size their persistent grids for (current device): all of them, or
  * BS_FP8_SM_LIMIT from the environment when that is smaller (SMs left to concurrent kernels). */

@@ -18,6 +18,7 @@ Outputs: golden.npz (arrays) and golden.json (metadata, hashes, the reference se
 from __future__ import annotations
 
 import argparse
+import os
 import ast
 import hashlib
 import importlib.util
@@ -58,8 +59,12 @@ def seeded_bf16(shape, seed, std=1.0):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BS_FP8_REFERENCE_TREE"),
+                    help="checkout of lexing-2026/ucloud-ai-infra (default: $BS_FP8_REFERENCE_TREE)")
     a = ap.parse_args()
+    if not a.ref:
+        print("pass --ref (or set BS_FP8_REFERENCE_TREE) to the reference checkout", file=sys.stderr)
+        return 1
     ref = Path(a.ref)
     if not (ref / "patches/fp8_hand_sm89.py").exists():
         print(f"reference not found at {ref}", file=sys.stderr)

@@ -1,6 +1,6 @@
 """GPU parity of every kernel against the CPU oracle (seeded inputs, identical bytes on both sides).
 
-Bars:
+Bars (the parity bars this path is held to):
   * byte kernels (group quant, tile pack): bit-exact;
   * bf16 GEMM outputs: max relative error <= 1e-2 against the fp32-accumulated oracle, with the
     relative floor 1e-3 * max|ref| (logs/artifacts/20261031_hand/bench_hand.py:75 style);
@@ -199,6 +199,24 @@ def test_gemm_bf16_matches_oracle(cuda_lib, M, N, K, tiled):
     assert C.dtype == torch.bfloat16 and tuple(C.shape) == (M, N)
     assert O.max_rel_error(C.cpu(), ref) <= GEMM_MAX_REL
     assert O.norm_rel_error(C.cpu(), ref) <= 4e-3
+
+
+def test_decode_workspace_reuse_across_shapes(cuda_lib):
+    """Decode calls of different widths share one cached workspace per stream: a narrow split-K call leaves
+    partial tiles behind, and a wider call right after (more weight tiles, hence more arrival counters) must
+    still see zeroed counters. Then the narrow shape again, and a fused call, on the same workspace."""
+    ops = _ops()
+    shapes = [(16, 1024, 5120, False), (16, 40960, 5120, False), (16, 1024, 5120, False), (8, 8192, 2048, True),
+              (3, 65536, 1024, False)]
+    for M, N, K, fused in shapes:
+        A, B, As, Bs, _ = O.make_gemm_case(M, N, K, seed=N + M, outlier_frac=0.05)
+        if fused:
+            Q, Qs = ops.gemm_silu_quant(*_dev(A, B, As, Bs))
+            _check_fused(Q, Qs, A, B, As, Bs)
+        else:
+            C = ops.gemm(*_dev(A, B, As, Bs))
+            ref = O.blockwise_matmul(A, B, As, Bs)
+            assert O.max_rel_error(C.cpu(), ref) <= GEMM_MAX_REL, (M, N, K)
 
 
 @pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (300, 768, 2048), (128, 256, 17408)])

@@ -91,10 +91,10 @@ def _decode_grid(sms, tiles, kb):
 
 
 def _decode_ws(M, N, K, fused, sms):
+    """A fixed 64 KB prefix of per-tile counters (the same for every shape), then the partial tiles."""
     tiles = N // 256 if fused else N // 128
     ntp = (M + 15) // 16 * 16
-    counters = (tiles * 4 + 255) // 256 * 256
-    return counters + _decode_grid(sms, tiles, K // 128) * 2 * (2 if fused else 1) * ntp * 128 * 4
+    return 65536 + _decode_grid(sms, tiles, K // 128) * 2 * (2 if fused else 1) * ntp * 128 * 4
 
 
 def test_workspace_size_formula(lib):
@@ -129,13 +129,32 @@ def test_env_switch_semantics(monkeypatch):
     _fresh_module(monkeypatch)
 
 
-def test_select_tiles():
+def test_select_tiles(lib):
+    """select() reports the library's launch plan: the kernel, block and grid that actually run."""
     from fp8_hand_b200 import select
-    assert select(34816, 1)["kind"] == "decode" and select(34816, 1)["NTP"] == 16
-    assert select(34816, 112)["NTP"] == 112
+    sms = lib.bs_fp8_num_sms() or 148
+    d = select(34816, 1, fused=True)
+    assert d["kind"] == "decode" and d["NTP"] == 16 and d["threads"] == 384 and d["warpgroups"] == 2
+    assert d["split"] == "tile" and d["grid"] == 136  # 136 gate/up tile pairs: one CTA each
+    assert select(34816, 112, fused=True)["NTP"] == 112
+    assert select(34816, 56, fused=True)["threads"] == 640  # four promotion warpgroups at 48..80 tokens
+    assert select(5120, 1, K=17408)["threads"] == 256 and select(5120, 56, K=17408)["threads"] == 384
+    assert select(5120, 1, K=17408)["split"] == "stream-k" and select(5120, 1, K=17408)["grid"] == sms
     assert select(6144, 128)["kind"] == "decode"
+    assert 2 <= select(6144, 128)["stages"] <= 12
     p = select(34816, 129)
-    assert p["kind"] == "prefill" and (p["BM"], p["BN"]) == (128, 256)
+    assert p["kind"] == "prefill" and (p["BM"], p["BN"]) == (128, 256) and p["cluster"] == 1
+    f = select(34816, 8192, fused=True)  # CTA pairs from 1024 rows, every M tile in one raster group
+    assert (f["BM"], f["cluster"], f["group_m"], f["group_n"], f["tiles"]) == (256, 2, 32, 0, 32 * 136)
+    assert f["grid"] == 2 * min(sms // 2, f["tiles"]) and f["stages"] == 4 and f["tmem_cols"] == 512
+    dn = select(5120, 8192, K=17408)  # activation panel 142.6 MB > L2, weights 89 MB fit: sweep rows
+    assert (dn["group_m"], dn["group_n"], dn["BM"]) == (0, 20, 128)
+    big = select(248320, 8192, K=5120)  # activation panel fits in L2: sweep columns
+    assert big["group_m"] == 64 and big["group_n"] == 0
+    both = select(32768, 8192, K=17408)  # neither fits: groups of 2048 rows
+    assert both["group_m"] == 16 and both["group_n"] == 0
+    with pytest.raises(RuntimeError):
+        select(34816 + 128, 8192, fused=True)  # fused N2 must be a multiple of 256
 
 
 class _Proj(torch.nn.Module):

@@ -69,6 +69,8 @@ def _worker(rank, world, port, q):
         out_chunked = tp.TensorParallelMLP(shard, compute=OracleCompute, chunks=3)(x)
         q.put((rank, (out_bf16, out_f32, out_chunked)))
     finally:
+        # rank 0 hosts the rendezvous store: no rank tears down before every rank is done with it
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -136,19 +136,34 @@ int pair_min_rows(bool fused) {
 // K ranges (every CTA holds one segment of one tile: one fix-up, none at a tile boundary).
 // Otherwise the stream-K split over one CTA per SM keeps every SM streaming equal bytes. Never
 // more CTAs than (tile, K block) units.
-int decode_grid(int num_sms, int tiles, int KB) {
-  if (tiles <= num_sms && 10 * tiles >= 9 * num_sms) return tiles;
-  if (tiles < num_sms) {
-    const int s = num_sms / tiles;
-    if (s >= 2 && s <= KB && 20 * tiles * s >= 19 * num_sms) return tiles * s;
+// *split (optional) receives the choice: 0 one CTA per tile, s > 0 equal K splits, -1 stream-K.
+int decode_grid(int num_sms, int tiles, int KB, int* split = nullptr) {
+  int sp = -1, grid;
+  if (tiles <= num_sms && 10 * tiles >= 9 * num_sms) {
+    sp = 0;
+    grid = tiles;
+  } else if (tiles < num_sms && num_sms / tiles >= 2 && num_sms / tiles <= KB &&
+             20 * tiles * (num_sms / tiles) >= 19 * num_sms) {
+    sp = num_sms / tiles;
+    grid = tiles * sp;
+  } else {
+    const long long units = static_cast<long long>(tiles) * KB;
+    grid = static_cast<int>(units < num_sms ? units : num_sms);
   }
-  const long long units = static_cast<long long>(tiles) * KB;
-  return static_cast<int>(units < num_sms ? units : num_sms);
+  if (split) *split = sp;
+  return grid;
 }
 
-size_t decode_ws_bytes(int G, int nwg, int ntp, int tiles) {
-  const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
-  return counters + static_cast<size_t>(G) * 2 * nwg * ntp * 128 * sizeof(float);
+// Decode workspace layout: a fixed prefix of kCounterBytes holds one arrival counter per weight tile (up to
+// kMaxDecodeTiles tiles), then the fp32 partial tiles of the split-K CTAs. The prefix does not depend on the
+// shape and the kernels leave every counter they use at zero, so one zero-filled workspace serves any sequence
+// of shapes (a layout sized by the tile count would put the counters of a wider call where a narrower call
+// left partial sums).
+constexpr int kMaxDecodeTiles = 16384;
+constexpr size_t kCounterBytes = static_cast<size_t>(kMaxDecodeTiles) * 4;
+
+size_t decode_ws_bytes(int G, int nwg, int ntp) {
+  return kCounterBytes + static_cast<size_t>(G) * 2 * nwg * ntp * 128 * sizeof(float);
 }
 
 // One-time per (kernel, device) preparation: opt in to the kernel's dynamic shared memory and,
@@ -239,6 +254,32 @@ int dispatch_decode(int ntp, const CUtensorMap& tmW, const CUtensorMap& tmX, con
   }
 }
 
+// Compile-time configuration of the decode kernel for `ntp` tokens: stages, threads, TMEM columns,
+// promotion warpgroups, dynamic shared memory. False for a token count no kernel is built for.
+template <bool FUSED, int NTP>
+void decode_cfg_fill(int* v) {
+  using C = bs::DecodeCfg<FUSED, NTP>;
+  v[0] = C::kStages;
+  v[1] = C::kThreads;
+  v[2] = C::kTmemCols;
+  v[3] = C::kPwg;
+  v[4] = C::kSmemBytes;
+}
+template <bool FUSED>
+bool decode_cfg_values(int ntp, int* v) {
+  switch (ntp) {
+    case 16: decode_cfg_fill<FUSED, 16>(v); return true;
+    case 32: decode_cfg_fill<FUSED, 32>(v); return true;
+    case 48: decode_cfg_fill<FUSED, 48>(v); return true;
+    case 64: decode_cfg_fill<FUSED, 64>(v); return true;
+    case 80: decode_cfg_fill<FUSED, 80>(v); return true;
+    case 96: decode_cfg_fill<FUSED, 96>(v); return true;
+    case 112: decode_cfg_fill<FUSED, 112>(v); return true;
+    case 128: decode_cfg_fill<FUSED, 128>(v); return true;
+    default: return false;
+  }
+}
+
 // Clusters of two of `kern` that fit on the device at once (0 if the query fails).
 template <auto kernel>
 int max_pair_clusters(int threads, int smem) {
@@ -289,10 +330,57 @@ int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::Gem
   return launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, s, "k_prefill launch", tmA, tmB, p);
 }
 
-// Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant / bs_fp8_gemm_reduce_multicast.
-int run_gemm(bool fused, const void* A, const void* B, void* out, const float* As, const float* Bs, float* qs,
-             int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream,
-             int out_mc = 0) {
+// Largest weight panel (N x K bytes) for which a prefill GEMM whose activation panel exceeds L2 sweeps rows
+// (each activation tile fetched once, the weights kept in L2): 96 MB of the 126 MB L2 by default, leaving
+// room for the activation tiles in flight. BS_FP8_ROW_SWEEP_MAX_MB, read once per process, replaces it (0
+// turns the row sweep off).
+long long row_sweep_max_bytes() {
+  static std::once_flag once;
+  static long long v = 96ll << 20;
+  std::call_once(once, [] {
+    const char* e = std::getenv("BS_FP8_ROW_SWEEP_MAX_MB");
+    if (e && *e) {
+      const long long mb = std::strtoll(e, nullptr, 10);
+      if (mb >= 0 && mb < (1ll << 20)) v = mb << 20;
+    }
+  });
+  return v;
+}
+
+// Tile walk of a prefill GEMM (M > 128): tile shape and raster.
+struct PrefillPlan {
+  bool pair;             // 256-row tiles on CTA pairs (cta_group::2)
+  int rows;              // output rows per tile
+  int num_m, num_n;      // tiles along M and N
+  int group_m, group_n;  // raster groups (see prefill_tile_coords)
+};
+
+PrefillPlan prefill_plan(bool fused, int M, int N, int K) {
+  PrefillPlan pl;
+  pl.pair = M >= pair_min_rows(fused);
+  pl.rows = pl.pair ? 256 : 128;
+  pl.num_m = (M + pl.rows - 1) / pl.rows;
+  pl.num_n = fused ? N / 256 : (N / 128 + 1) / 2;
+  const long long a_bytes = static_cast<long long>(M) * K, b_bytes = static_cast<long long>(N) * K;
+  if (a_bytes <= (48ll << 20)) {
+    // the whole activation panel stays in L2: sweep every M tile down each weight column tile
+    pl.group_m = pl.num_m;
+    pl.group_n = 0;
+  } else if (b_bytes <= row_sweep_max_bytes()) {
+    // the weights stay in L2: sweep every N tile along each activation row block
+    pl.group_m = 0;
+    pl.group_n = pl.num_n;
+  } else {
+    pl.group_m = 2048 / pl.rows;
+    pl.group_n = 0;
+  }
+  return pl;
+}
+
+// Argument, pointer and alignment checks shared by every GEMM entry point (BS_OK for M == 0 too; the
+// callers return before launching anything then).
+int validate_gemm(bool fused, const void* A, const void* B, const void* out, const float* As, const float* Bs,
+                  const float* qs, int M, int N, int K, int ldc, int b_tiled, int out_dtype) {
   if (M < 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0) return BS_ERR_ARG;
   if (fused && N % 256 != 0) return BS_ERR_ARG;
   if (!fused && (ldc < N || ldc % 8 != 0 || (out_dtype != 0 && out_dtype != 1))) return BS_ERR_ARG;
@@ -300,6 +388,15 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   if (M == 0) return BS_OK;
   if (!A || !B || !out || !As || !Bs || (fused && !qs)) return BS_ERR_ARG;
   if (!aligned16(A) || !aligned16(B) || !aligned16(out)) return BS_ERR_ALIGN;
+  return BS_OK;
+}
+
+// Shared body of bs_fp8_gemm / bs_fp8_gemm_silu_quant / bs_fp8_gemm_reduce_multicast.
+int run_gemm(bool fused, const void* A, const void* B, void* out, const float* As, const float* Bs, float* qs,
+             int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream,
+             int out_mc = 0) {
+  const int vrc = validate_gemm(fused, A, B, out, As, Bs, qs, M, N, K, ldc, b_tiled, out_dtype);
+  if (vrc != BS_OK || M == 0) return vrc;
   DeviceState* d = device_state();
   if (!d) return BS_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -331,11 +428,11 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
     const int grid = decode_grid(d->num_sms, tiles, K / 128);
     // the kernel indexes (tile, K block) units with 32-bit products unit * grid
     if (static_cast<long long>(tiles) * (K / 128) * grid >= (1ll << 31)) return BS_ERR_ARG;
-    const size_t need = decode_ws_bytes(grid, nwg, ntp, tiles);
+    if (tiles > kMaxDecodeTiles) return BS_ERR_ARG;
+    const size_t need = decode_ws_bytes(grid, nwg, ntp);
     if (!ws || ws_bytes < need || !aligned16(ws)) return BS_ERR_WORKSPACE;
-    const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
     p.cnt = static_cast<int*>(ws);
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + counters);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
     CUtensorMap tmX;
     if (make_map(&tmX, A, K, M, K, 128, ntp) != BS_OK) return BS_ERR_TMAP;
     if (!fused) return dispatch_decode<false>(ntp, tmB, tmX, tmX, p, grid, s);
@@ -347,19 +444,15 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
 
   CUtensorMap tmA;
   if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
-  const int num_n = fused ? N / 256 : (N / 128 + 1) / 2;
-  // 256-row tiles on CTA pairs once there are enough rows for them
-  const bool pair = M >= pair_min_rows(fused);
-  const int rows = pair ? 256 : 128;
-  const int num_m = (M + rows - 1) / rows;
-  // Raster: one group over every M tile when the whole A panel stays in L2 (each weight tile is then
-  // read from HBM once), else groups of 2048 rows.
-  p.group_m = static_cast<long long>(M) * K <= (48ll << 20) ? num_m : 2048 / rows;
-  if (pair)
-    return fused ? launch_prefill<true, true>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
-                 : launch_prefill<false, true>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
-  return fused ? launch_prefill<true, false>(tmA, tmB, p, num_m * num_n, d->num_sms, s)
-               : launch_prefill<false, false>(tmA, tmB, p, num_m * num_n, d->num_sms, s);
+  const PrefillPlan pl = prefill_plan(fused, M, N, K);
+  p.group_m = pl.group_m;
+  p.group_n = pl.group_n;
+  const int tiles = pl.num_m * pl.num_n;
+  if (pl.pair)
+    return fused ? launch_prefill<true, true>(tmA, tmB, p, tiles, d->num_sms, s)
+                 : launch_prefill<false, true>(tmA, tmB, p, tiles, d->num_sms, s);
+  return fused ? launch_prefill<true, false>(tmA, tmB, p, tiles, d->num_sms, s)
+               : launch_prefill<false, false>(tmA, tmB, p, tiles, d->num_sms, s);
 }
 
 // ------------------------------------------------------------ allocation-free GEMM entry point
@@ -427,18 +520,22 @@ int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* A
 int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
                         int ldc, int b_tiled, int out_dtype, void* stream) {
   // Shapes above 128 rows run the prefill kernel, which needs no scratch; decode shapes use the
-  // static array, and are refused when their scratch would not fit in it.
-  if (M <= 128 && M > 0 && N > 0 && K > 0 && K % 128 == 0 && N % 128 == 0) {
+  // static array, and are refused when their scratch would not fit in it. A call that is refused
+  // touches nothing: every check runs before the counters are cleared.
+  const int vrc = validate_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype);
+  if (vrc != BS_OK || M == 0) return vrc;
+  if (M <= 128) {
     void* scratch = nullptr;
     const int rc = noalloc_scratch(&scratch);
     if (rc != BS_OK) return rc;
     DeviceState* d = device_state();
     if (!d) return BS_ERR_CUDA;
     const int tiles = N / 128;
-    const size_t need = decode_ws_bytes(decode_grid(d->num_sms, tiles, K / 128), 1, ntp_for(M), tiles);
+    if (tiles > kMaxDecodeTiles) return BS_ERR_ARG;
+    const size_t need = decode_ws_bytes(decode_grid(d->num_sms, tiles, K / 128), 1, ntp_for(M));
     if (need > kNoAllocScratchBytes) return BS_ERR_SCRATCH;
-    // The array keeps the previous call's contents; the counters must start at zero.
-    const size_t counters = ((static_cast<size_t>(tiles) * 4 + 255) / 256) * 256;
+    // The array keeps the previous call's contents; the counters this call uses must start at zero.
+    const size_t counters = static_cast<size_t>(tiles) * 4;
     const cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc counters)");
     return run_gemm(false, A, B, C, As, Bs, nullptr, M, N, K, ldc, b_tiled, out_dtype, scratch,
@@ -459,7 +556,8 @@ size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {
   DeviceState* d = device_state();
   const int sms = d ? d->num_sms : 148;
   const int tiles = fused ? N / 256 : N / 128;
-  return decode_ws_bytes(decode_grid(sms, tiles, K / 128), fused ? 2 : 1, ntp_for(M), tiles);
+  if (tiles > kMaxDecodeTiles) return 0;
+  return decode_ws_bytes(decode_grid(sms, tiles, K / 128), fused ? 2 : 1, ntp_for(M));
 }
 
 int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K, void* stream) {
@@ -534,6 +632,59 @@ int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
   cudaGetLastError();
   k_selftest_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, d->status);
   return launch_status("k_selftest_wait launch");
+}
+
+int bs_fp8_launch_plan(int M, int N, int K, int fused, int* plan, int n) {
+  if (!plan || n < BS_PLAN_FIELDS) return BS_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 || N % (fused ? 256 : 128)) return BS_ERR_ARG;
+  for (int i = 0; i < n; ++i) plan[i] = 0;
+  DeviceState* d = device_state();
+  const int sms = d ? d->num_sms : 148;
+  const int KB = K / 128;
+  if (M <= 128) {
+    const int ntp = ntp_for(M);
+    const int tiles = fused ? N / 256 : N / 128;
+    int split = 0;
+    const int grid = decode_grid(sms, tiles, KB, &split);
+    int cfg[5];
+    if (!(fused ? decode_cfg_values<true>(ntp, cfg) : decode_cfg_values<false>(ntp, cfg))) return BS_ERR_ARG;
+    plan[BS_PLAN_KIND] = 1;
+    plan[BS_PLAN_TILE_ROWS] = 128;  // weight rows (swap-AB: the weights are the MMA's M side)
+    plan[BS_PLAN_TILE_COLS] = ntp;  // tokens, padded to a multiple of 16
+    plan[BS_PLAN_STAGES] = cfg[0];
+    plan[BS_PLAN_THREADS] = cfg[1];
+    plan[BS_PLAN_GRID] = grid;
+    plan[BS_PLAN_CLUSTER] = 1;
+    plan[BS_PLAN_TMEM_COLS] = cfg[2];
+    plan[BS_PLAN_SPLIT] = split;
+    plan[BS_PLAN_WARPGROUPS] = cfg[3];
+    plan[BS_PLAN_SMEM] = cfg[4];
+    return BS_OK;
+  }
+  const PrefillPlan pl = prefill_plan(fused != 0, M, N, K);
+  const int tiles = pl.num_m * pl.num_n;
+  plan[BS_PLAN_KIND] = 2;
+  plan[BS_PLAN_TILE_ROWS] = pl.rows;
+  plan[BS_PLAN_TILE_COLS] = 256;
+  if (pl.pair) {
+    plan[BS_PLAN_STAGES] = fused ? bs::PrefillCfg<true, true>::kStages : bs::PrefillCfg<false, true>::kStages;
+    plan[BS_PLAN_SMEM] = fused ? bs::PrefillCfg<true, true>::kSmemBytes : bs::PrefillCfg<false, true>::kSmemBytes;
+    const int pairs = (sms / 2 < tiles) ? sms / 2 : tiles;
+    plan[BS_PLAN_GRID] = 2 * pairs;
+    plan[BS_PLAN_CLUSTER] = 2;
+  } else {
+    plan[BS_PLAN_STAGES] = fused ? bs::PrefillCfg<true, false>::kStages : bs::PrefillCfg<false, false>::kStages;
+    plan[BS_PLAN_SMEM] = fused ? bs::PrefillCfg<true, false>::kSmemBytes : bs::PrefillCfg<false, false>::kSmemBytes;
+    plan[BS_PLAN_GRID] = tiles < sms ? tiles : sms;
+    plan[BS_PLAN_CLUSTER] = 1;
+  }
+  plan[BS_PLAN_THREADS] = bs::PrefillCfg<false, false>::kThreads;
+  plan[BS_PLAN_GROUP_M] = pl.group_m;
+  plan[BS_PLAN_GROUP_N] = pl.group_n;
+  plan[BS_PLAN_TMEM_COLS] = bs::PrefillCfg<false, false>::kTmemCols;
+  plan[BS_PLAN_WARPGROUPS] = 2;
+  plan[BS_PLAN_TILES] = tiles;
+  return BS_OK;
 }
 
 int bs_fp8_num_sms(void) {

@@ -36,6 +36,7 @@ SIGNATURES = {
     "bs_fp8_pack_tiles": (_I, [_VP, _VP, _I, _I, _VP]),
     "bs_fp8_status": (_I, [ctypes.POINTER(_I), _I]),
     "bs_fp8_selftest_wait_timeout": (_I, [_U64, _VP]),
+    "bs_fp8_launch_plan": (_I, [_I, _I, _I, _I, ctypes.POINTER(_I), _I]),
     "bs_fp8_num_sms": (_I, []),
     "bs_fp8_error_string": (ctypes.c_char_p, [_I]),
     "bs_fp8_abi_version": (_I, []),
@@ -135,6 +136,18 @@ def reset_workspaces() -> None:
     """Zero every cached workspace (needed only after a kernel reported a timeout)."""
     for buf in _WS.values():
         buf.zero_()
+
+
+PLAN_FIELDS = ("kind", "tile_rows", "tile_cols", "stages", "threads", "grid", "cluster", "group_m", "group_n",
+               "tmem_cols", "split", "warpgroups", "smem_bytes", "tiles")  # include/bs_fp8.h BS_PLAN_*
+
+
+def launch_plan(M: int, N: int, K: int, fused: bool) -> dict:
+    """What the library launches for an M x N x K GEMM (fused: the gate_up front half) on the current device."""
+    buf = (ctypes.c_int * len(PLAN_FIELDS))()
+    check(lib().bs_fp8_launch_plan(int(M), int(N), int(K), int(bool(fused)), buf, len(PLAN_FIELDS)),
+          "bs_fp8_launch_plan")
+    return dict(zip(PLAN_FIELDS, list(buf)))
 
 
 def num_sms() -> int:

@@ -41,16 +41,30 @@ FUSED_MIN_M = int(os.getenv("SGLANG_FP8_HAND_FUSED_MIN_M", "1"))
 BK = 128
 CAPABILITY = (10, 0)
 DECODE_MAX_M = 128           # M <= 128 runs the swap-AB split-K kernel
-PREFILL = dict(kind="prefill", BM=128, BN=256, BK=BK, stages=4, group_m=16, threads=384)
 
 
-def select(N: int, M: int) -> dict:
-    """Tile of an M x N product: the prefill tcgen05 tile for M > 128, else the decode
-    (swap-AB, weights as the MMA's M=128 side, tokens padded to a multiple of 16)."""
-    if M > DECODE_MAX_M:
-        return dict(PREFILL)
-    ntp = max(16, (M + 15) // 16 * 16)
-    return dict(kind="decode", BM=BK, NTP=ntp, BK=BK, split="stream-k", threads=256)
+def select(N: int, M: int, K: int = 5120, fused: bool = False) -> dict:
+    """The kernel an M x N product (K deep; fused: the gate_up front half, N = 2I) launches, read from the
+    library's own launch plan (bs_fp8_launch_plan), so the values are the ones that run: the reference's
+    select(N, M) reported its sm_89 tile the same way (H:74-81). Keys:
+      kind       "decode" (M <= 128: swap-AB, the weights are the MMA's 128-row side, tokens its N side)
+                 or "prefill" (persistent tcgen05 tiles)
+      BM, BN, BK tile: decode 128 weight rows x NTP tokens; prefill 128 or 256 (CTA pairs) rows x 256 columns
+      NTP        decode: tokens padded to a multiple of 16
+      stages, threads, grid, cluster, tmem_cols, smem_bytes, warpgroups (promotion)
+      split      decode: "tile" (one CTA per weight tile), "k<s>" (s equal K splits) or "stream-k"
+      group_m / group_n   prefill raster: M tiles per group (column sweep) / N tiles per group (row sweep)
+    """
+    p = _native.launch_plan(M, N, K, fused)
+    out = dict(BK=BK, stages=p["stages"], threads=p["threads"], grid=p["grid"], cluster=p["cluster"],
+               tmem_cols=p["tmem_cols"], smem_bytes=p["smem_bytes"], warpgroups=p["warpgroups"])
+    if p["kind"] == 1:
+        split = {0: "tile", -1: "stream-k"}.get(p["split"], f"k{p['split']}")
+        out.update(kind="decode", BM=p["tile_rows"], BN=p["tile_cols"], NTP=p["tile_cols"], split=split)
+    else:
+        out.update(kind="prefill", BM=p["tile_rows"], BN=p["tile_cols"], group_m=p["group_m"],
+                   group_n=p["group_n"], tiles=p["tiles"])
+    return out
 
 
 def precompile() -> list[str]:

@@ -20,6 +20,9 @@ B200-side extension the north star asks for:
            rank's copy (bs_fp8_gemm_reduce_multicast), so the reduction overlaps the GEMM tile by tile.
            A one-element NCCL all_reduce orders the zeroing of the copies before the GEMMs and the GEMMs
            before the result is read. `chunks` does not apply: the reduction already overlaps the GEMM.
+           Two ranks only: the switch adds the ranks' bf16 partials into each copy in no fixed order, which
+           for two partials (0 + a + b) always rounds the same way, but for three or more can round
+           differently in different ranks' copies and leave the replicas unequal.
 
 The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
 the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
@@ -87,7 +90,9 @@ class TensorParallelMLP:
     """x [M, H] bf16 (replicated) -> quant -> fused gate_up_r -> down_r -> all_reduce -> [M, H]."""
 
     def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.bfloat16, compute=None,
-                 chunks: int = 1, reduce: str = "nccl"):
+                 chunks: int = 1, reduce: str = "nccl", return_buffer: bool = False):
+        """reduce="multimem" returns a copy of the shared output buffer unless return_buffer=True, in which case
+        the caller gets the buffer's row view itself and must consume it before the next call overwrites it."""
         if compute is None:
             from . import ops as compute
         if reduce not in ("nccl", "multimem"):
@@ -100,8 +105,12 @@ class TensorParallelMLP:
         self.compute = compute
         self.chunks = max(1, int(chunks))
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if reduce == "multimem" and self.world > 2:
+            raise ValueError("reduce='multimem' needs exactly two ranks: with three or more the switch's bf16 "
+                             "additions can round differently in different ranks' copies")
         self.reduce = reduce if self.world > 1 else "nccl"
-        self._mc: dict[int, tuple] = {}  # rows -> (this rank's output copy, symmetric-memory handle, mc address)
+        self.return_buffer = return_buffer
+        self._mc = None  # (output buffer [rows, n], symmetric-memory handle, multicast address of row 0)
         self._flag = None
 
     def _sync(self, device) -> None:
@@ -111,17 +120,24 @@ class TensorParallelMLP:
         dist.all_reduce(self._flag, group=self.group)
 
     def multicast_out(self, m: int, n: int, device) -> tuple:
-        """This rank's copy of the [m, n] bf16 output in symmetric memory and its multicast address
-        (collective: every rank calls it with the same m on its first use)."""
-        if m not in self._mc:
+        """Rows [0, m) of this rank's copy of the bf16 output buffer in symmetric memory, with the multicast
+        address of its row 0. One buffer serves every row count: rows are contiguous with stride n, so row 0's
+        multicast address maps any leading row view. It is allocated (collectively: every rank calls this
+        with the same m) on first use and when a larger m arrives, then at least doubling, so serving with
+        varying batch sizes allocates O(log M) times and never keeps more than one buffer."""
+        buf = self._mc
+        if buf is None or m > buf[0].shape[0] or n != buf[0].shape[1]:
             import torch.distributed._symmetric_memory as symm_mem
-            out = symm_mem.empty(m, n, dtype=torch.bfloat16, device=device)
+            rows = m if buf is None or n != buf[0].shape[1] else max(m, 2 * buf[0].shape[0])
+            self._mc = None
+            out = symm_mem.empty(rows, n, dtype=torch.bfloat16, device=device)
             handle = symm_mem.rendezvous(out, self.group if self.group is not None else dist.group.WORLD)
             base = handle.multicast_ptr
             if not base:
                 raise RuntimeError("the group has no NVSwitch multicast mapping (NVLS)")
-            self._mc[m] = (out, handle, base + (out.data_ptr() - handle.buffer_ptrs[handle.rank]))
-        return self._mc[m]
+            self._mc = (out, handle, base + (out.data_ptr() - handle.buffer_ptrs[handle.rank]))
+        out, handle, mc = self._mc
+        return out[:m], handle, mc
 
     def partial(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's [M, H] contribution (before the reduction)."""
@@ -137,8 +153,6 @@ class TensorParallelMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if self.reduce == "multimem":
-            # The returned tensor is this rank's copy of the buffer: the next call with the same row count
-            # overwrites it.
             c, s = self.compute, self.shard
             out, _, mc = self.multicast_out(x.shape[0], s.down.shape[0] * (BLOCK if s.tiled else 1), x.device)
             out.zero_()
@@ -147,7 +161,7 @@ class TensorParallelMLP:
             Q, Qs = c.gemm_silu_quant(A, s.gate_up, As, s.gate_up_scale, b_tiled=s.tiled)
             c.gemm_reduce_multicast(Q, s.down, Qs, s.down_scale, out, mc, b_tiled=s.tiled)
             self._sync(x.device)
-            return out
+            return out if self.return_buffer else out.clone()
         if self.world == 1 or self.chunks == 1 or x.shape[0] <= BLOCK:
             part = self.partial(x)
             if self.world > 1:
