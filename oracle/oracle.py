@@ -56,32 +56,42 @@ def group_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
     """RMSNorm then the per-token-group quant, with the rounding points of the unfused pair (the bf16 norm
     output, then quant_block) and the library kernel's fixed fp32 summation order for sum(h^2), which
-    depends on K only: thread t of a 256-thread row adds the squares of its elements 8(t + 256j) + e in
-    (j, e) order; each 32-thread warp combines its threads in a butterfly (xor 16, 8, 4, 2, 1); then
-    ss = ((w0 + w1) + w2) + ... + w7. rs = 1 / sqrt(ss / K + eps) in IEEE fp32; y = bf16((h * rs) * w).
+    depends on K only. A row belongs to W warps (the smallest power of two, at most 8, that leaves each thread
+    at most 8 of the row's K/8 16-byte chunks); thread t of its 32W threads holds the chunks c = t + 32W j and
+    keeps two partial sums, of its even and of its odd elements: for its chunks in increasing c and
+    e = 0..3, even += h[8c + 2e]^2 and odd += h[8c + 2e + 1]^2 (each square rounded, then each add); its
+    total is even + odd; each 32-thread warp combines its threads in a butterfly (xor 16, 8, 4, 2, 1); the
+    row's sum is the W warp totals added in warp order.
+    rs = 1 / sqrt(ss / K + eps) in IEEE fp32; y = bf16((h * rs) * w).
     With residual: h = bf16(x + residual), which is also returned (the fused add writes it back).
     Returns (A, As, h_bf16 or None)."""
     xf = x.float()
     h = (xf + residual.float()).to(torch.bfloat16).float() if residual is not None else xf
     M, K = h.shape
     nch = K // 8
+    W = 1
+    while W < 8 and nch > 32 * W * 8:
+        W *= 2
+    T = 32 * W
     hn = h.numpy().astype(np.float32)
-    sq = hn * hn  # fp32 products, rounded once
-    threads = np.zeros((M, 256), dtype=np.float32)
-    tid = np.arange(256)
-    for j in range((nch + 255) // 256):
-        c = 256 * j + tid
+    sq = (hn * hn).astype(np.float32)  # fp32 products, rounded once
+    even = np.zeros((M, T), dtype=np.float32)
+    odd = np.zeros((M, T), dtype=np.float32)
+    tid = np.arange(T)
+    for j in range((nch + T - 1) // T):
+        c = T * j + tid
         live = c < nch
-        for e in range(8):
-            cols = np.where(live, c * 8 + e, 0)
-            add = np.where(live[None, :], sq[:, cols], np.float32(0))
-            threads = np.where(live[None, :], threads + add, threads).astype(np.float32)
-    warps = threads.reshape(M, 8, 32)
+        for e in range(4):
+            ce = np.where(live, c * 8 + 2 * e, 0)
+            even = np.where(live[None, :], even + sq[:, ce], even).astype(np.float32)
+            odd = np.where(live[None, :], odd + sq[:, ce + 1], odd).astype(np.float32)
+    threads = (even + odd).astype(np.float32)
+    warps = threads.reshape(M, W, 32)
     lane = np.arange(32)
     for o in (16, 8, 4, 2, 1):
         warps = (warps + warps[:, :, lane ^ o]).astype(np.float32)
     ss = warps[:, 0, 0]
-    for i in range(1, 8):
+    for i in range(1, W):
         ss = (ss + warps[:, i, 0]).astype(np.float32)
     rs = np.float32(1) / np.sqrt((ss / np.float32(K) + np.float32(eps)).astype(np.float32))
     rs_t = torch.from_numpy(rs.astype(np.float32))

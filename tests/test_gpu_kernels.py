@@ -45,6 +45,31 @@ def test_group_quant_bit_exact(cuda_lib, M, K):
     assert torch.equal(As.cpu(), sr)
 
 
+@pytest.mark.parametrize("order", ["sorted", "shuffled"])
+def test_group_quant_every_bf16_value(cuda_lib, order):
+    """Every finite bf16 value quantised in 128-groups whose maximum is the group's own largest value or up to
+    2^5 above it: bytes and scales equal the oracle's quantiser (IEEE division x / s; the kernel divides with
+    a correctly rounded reciprocal and one correction step). Sorted groups hold values of similar magnitude,
+    so their quotients cover the whole e4m3 range."""
+    vals = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    finite = vals[torch.isfinite(vals.float())].float()
+    g = torch.Generator().manual_seed(5)
+    body = finite[finite.abs().argsort()] if order == "sorted" else finite[torch.randperm(len(finite), generator=g)]
+    n = len(body) // 127 * 127
+    body = body[:n].view(-1, 127)
+    gmax = body.abs().amax(dim=1, keepdim=True)
+    shift = torch.randint(0, 6, gmax.shape, generator=g).float()
+    shift = torch.where(gmax > 1e36, torch.zeros_like(shift), shift)
+    lead = gmax * torch.exp2(shift) * torch.where(torch.rand(gmax.shape, generator=g) < 0.5, -1.0, 1.0)
+    x = torch.cat([lead, body], dim=1).to(torch.bfloat16)
+    rows = x.shape[0] // 4 * 4
+    x = x[:rows].reshape(rows // 4, 512)
+    A, As = _ops().group_quant(x.cuda())
+    qr, sr = O.group_quant(x)
+    assert torch.equal(A.cpu().view(torch.uint8), qr.view(torch.uint8))
+    assert torch.equal(As.cpu(), sr)
+
+
 def test_group_quant_strided_rows(cuda_lib):
     x = O.make_activation(16, 1024, seed=5)
     big = torch.zeros(16, 1536, dtype=torch.bfloat16)

@@ -97,11 +97,12 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, u
   return r == CUDA_SUCCESS ? BS_OK : BS_ERR_TMAP;
 }
 
-// Weight map: tile-first [N*K/128 rows of 128 bytes] or row-major [N rows of K bytes].
-int make_weight_map(CUtensorMap* m, const void* B, int N, int K, int tiled) {
+// Weight map: tile-first [N*K/128 rows of 128 bytes] or row-major [N rows of K bytes], with boxes of
+// `box_rows` weight rows x 128 bytes (128: whole weight blocks; 64: the fused prefill's half blocks).
+int make_weight_map(CUtensorMap* m, const void* B, int N, int K, int tiled, int box_rows = 128) {
   if (tiled)
-    return make_map(m, B, 128, static_cast<uint64_t>(N) * (K / 128), 128, 128, 128);
-  return make_map(m, B, K, N, K, 128, 128);
+    return make_map(m, B, 128, static_cast<uint64_t>(N) * (K / 128), 128, 128, box_rows);
+  return make_map(m, B, K, N, K, 128, box_rows);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -444,6 +445,8 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
 
   CUtensorMap tmA;
   if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
+  // the fused kernel interleaves gate and up weight rows in 64-row halves
+  if (fused && make_weight_map(&tmB, B, N, K, b_tiled, 64) != BS_OK) return BS_ERR_TMAP;
   const PrefillPlan pl = prefill_plan(fused, M, N, K);
   p.group_m = pl.group_m;
   p.group_n = pl.group_n;
@@ -501,6 +504,34 @@ __global__ void k_selftest_wait(uint64_t limit_ns, int* status) {
   if (threadIdx.x == 0) bs::mbar_wait(&bar, 0, &abort_flag, status, bs::kErrTimeoutSelftest, limit_ns);
 }
 
+}  // namespace
+
+namespace {
+using RowKernel = void (*)(const __nv_bfloat16*, int, __nv_bfloat16*, int, const __nv_bfloat16*, float, uint8_t*,
+                           float*, int, int);
+// Warps per row of k_row_group_quant: the smallest power of two that leaves each thread at most kRowChunks
+// 16-byte chunks (K <= 16384).
+int row_warps(int K) {
+  const int nch = K / 8;
+  int W = 1;
+  while (W < 8 && nch > 32 * W * bs::kRowChunks) W *= 2;
+  return W;
+}
+template <bool NORM, bool RES>
+RowKernel row_kernel(int W) {
+  return W == 1 ? bs::k_row_group_quant<1, NORM, RES>
+         : W == 2 ? bs::k_row_group_quant<2, NORM, RES>
+         : W == 4 ? bs::k_row_group_quant<4, NORM, RES>
+                  : bs::k_row_group_quant<8, NORM, RES>;
+}
+int launch_row_quant(RowKernel kern, int W, const void* x, int ldx, void* residual, int ldr, const void* weight,
+                     float eps, void* A, float* As, int M, int K, void* stream, const char* where) {
+  const int rows_per_cta = bs::kNormThreads / 32 / W;
+  const int grid = (M + rows_per_cta - 1) / rows_per_cta;
+  return launch_pdl(kern, grid, bs::kNormThreads, 0, static_cast<cudaStream_t>(stream), where,
+                    static_cast<const __nv_bfloat16*>(x), ldx, static_cast<__nv_bfloat16*>(residual), ldr,
+                    static_cast<const __nv_bfloat16*>(weight), eps, static_cast<uint8_t*>(A), As, M, K);
+}
 }  // namespace
 
 extern "C" {
@@ -567,6 +598,13 @@ int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K,
   if (!aligned16(x) || !aligned16(A)) return BS_ERR_ALIGN;
   DeviceState* d = device_state();
   if (!d) return BS_ERR_CUDA;
+  if (K <= bs::kNormMaxK) {
+    // rows held whole by one to eight warps: every load of a thread in flight at once
+    const int W = row_warps(K);
+    return launch_row_quant(row_kernel<false, false>(W), W, x, ldx, nullptr, K, nullptr, 0.f, A, As, M, K, stream,
+                            "k_row_group_quant launch");
+  }
+  // wider rows: sixteen threads per 128-group, grid-stride over the groups
   const long long groups = static_cast<long long>(M) * (K / 128);
   const int per_block = bs::kQuantThreads / 16;
   long long blocks = (groups + per_block - 1) / per_block;
@@ -585,18 +623,11 @@ int bs_fp8_rmsnorm_group_quant(const void* x, int ldx, void* residual, int ldr, 
   if (M == 0) return BS_OK;
   if (!x || !weight || !A || !As) return BS_ERR_ARG;
   if (!aligned16(x) || !aligned16(weight) || !aligned16(A) || (residual && !aligned16(residual))) return BS_ERR_ALIGN;
-  if (K > bs::kNormThreads * 8 * bs::kNormMaxRounds) return BS_ERR_ARG;
+  if (K > bs::kNormMaxK) return BS_ERR_ARG;
   if (!device_state()) return BS_ERR_CUDA;
-  // registers scale with the chunks each thread holds, so the kernel is built per round count
-  const int rounds = (K / 8 + bs::kNormThreads - 1) / bs::kNormThreads;
-  auto kern = rounds <= 1 ? bs::k_rmsnorm_group_quant<1>
-              : rounds <= 2 ? bs::k_rmsnorm_group_quant<2>
-              : rounds <= 3 ? bs::k_rmsnorm_group_quant<3>
-              : rounds <= 4 ? bs::k_rmsnorm_group_quant<4>
-                            : bs::k_rmsnorm_group_quant<8>;
-  return launch_pdl(kern, M, bs::kNormThreads, 0, static_cast<cudaStream_t>(stream), "k_rmsnorm_group_quant launch",
-                    static_cast<const __nv_bfloat16*>(x), ldx, static_cast<__nv_bfloat16*>(residual), ldr,
-                    static_cast<const __nv_bfloat16*>(weight), eps, static_cast<uint8_t*>(A), As, M, K);
+  const int W = row_warps(K);
+  return launch_row_quant(residual ? row_kernel<true, true>(W) : row_kernel<true, false>(W), W, x, ldx, residual,
+                          ldr, weight, eps, A, As, M, K, stream, "k_row_group_quant<norm> launch");
 }
 
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {

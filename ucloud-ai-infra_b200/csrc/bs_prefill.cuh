@@ -10,9 +10,10 @@
 //
 // CTA layout (384 threads, one persistent CTA per SM):
 //   warps 0-7  promotion + epilogue. Warp w reads TMEM lanes 32*(w%4)..+31 (one tile row per
-//              thread) and columns 128*(w/4)..+127, i.e. exactly one 128-wide weight block, so
-//              the scale product is one scalar per thread per K block.
-//   warp 8     TMA producer: A box 128x128 and two weight boxes 128x128 per K block.
+//              thread) and columns 128*(w/4)..+127: one 128-wide weight block (plain), so the scale
+//              product is one scalar per thread per K block, or 64 gate and 64 up columns (fused), two.
+//   warp 8     TMA producer: A box 128x128 and 256 weight rows x 128 bytes per K block (two 128-row
+//              boxes; fused: four 64-row boxes).
 //   warp 9     TMEM allocator + MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32) per K block
 //              into one of two TMEM partial buffers (2 x 256 columns = all 512).
 //   warps 10-11 idle; warps 8-11 form the warpgroup that hands its registers to warps 0-7
@@ -21,9 +22,10 @@
 // promotion warps fold block kb into their register accumulators.
 //
 // FUSED=true is the gate_up + SiLU*up + per-token-group quant kernel (reference
-// patches/fp8_hand_sm89.py:314-583): the 256 MMA columns are gate block j and up block
-// j + I/128 (I = N/2), the up accumulators cross to the gate warps through shared memory, and
-// each gate thread owns a whole 128-wide quant group of its row:
+// patches/fp8_hand_sm89.py:314-583): the 256 MMA columns are [gate 0-63 | up 0-63 | gate 64-127 |
+// up 64-127] of gate block j and up block j + I/128 (I = N/2), loaded as 64-row weight boxes, so each
+// promotion thread holds gate and up of the same 64 output columns and forms y without any exchange; the
+// two warpgroups meet only to take the 128-wide quant group's amax:
 //   y = silu(g) * u;  scale = max(amax|y|, 1e-10) / 448;  q = sat_e4m3(y * (1 / scale)).
 #pragma once
 #include <type_traits>
@@ -53,12 +55,13 @@ template <bool FUSED, bool PAIR = false>
 struct PrefillCfg {
   using Regs = RegSplit<384, 168, 40, 232>;
   static constexpr int kThreads = Regs::kThreads;
-  static constexpr int kStages = PAIR ? (FUSED ? 4 : 6) : (FUSED ? 3 : 4);
+  static constexpr int kStages = PAIR ? 6 : 4;
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = (PAIR ? 128 : 256) * 128;  // a pair CTA holds half of the weight rows
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // fused: half groups + amax halves; plain: a 4 KB row-transpose buffer per promotion warp (multicast output)
-  static constexpr int kXchBytes = FUSED ? 128 * 128 * 4 + 128 * 2 * 4 : 8 * 4096;
+  // fused: the two warpgroups' amax halves per row; plain: a 4 KB row-transpose buffer per promotion warp
+  // (multicast output)
+  static constexpr int kXchBytes = FUSED ? 128 * 2 * 4 : 8 * 4096;
   static constexpr int kBarOff = kStages * kStageBytes + kXchBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers, then slack for 1 KB alignment
   static constexpr int kTmemCols = 512;
@@ -108,6 +111,22 @@ __device__ __forceinline__ void load_weight_box_pair(void* dst, const CUtensorMa
     tma_load_2d_pair(dst, map, bar, 0, (nb * KB + kb) * 128, policy);
   else
     tma_load_2d_pair(dst, map, bar, kb * 128, nb * 128, policy);
+}
+
+// Rows 64h .. 64h+63 of the weight box (nb, kb), through a map whose box is 64 rows high.
+__device__ __forceinline__ void load_weight_half(void* dst, const CUtensorMap* map, uint64_t* bar, int nb, int h,
+                                                 int kb, int KB, int tiled, uint64_t policy) {
+  if (tiled)
+    tma_load_2d(dst, map, bar, 0, (nb * KB + kb) * 128 + 64 * h, policy);
+  else
+    tma_load_2d(dst, map, bar, kb * 128, nb * 128 + 64 * h, policy);
+}
+__device__ __forceinline__ void load_weight_half_pair(void* dst, const CUtensorMap* map, uint32_t bar, int nb, int h,
+                                                      int kb, int KB, int tiled, uint64_t policy) {
+  if (tiled)
+    tma_load_2d_pair(dst, map, bar, 0, (nb * KB + kb) * 128 + 64 * h, policy);
+  else
+    tma_load_2d_pair(dst, map, bar, kb * 128, nb * 128 + 64 * h, policy);
 }
 
 __device__ __forceinline__ void prefetch_weight_box(const CUtensorMap* map, int nb, int kb, int KB, int tiled) {
@@ -216,12 +235,29 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
             const uint32_t lead_full = mapa_shared(&full[s], 0);
             if (cr == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
             tma_load_2d_pair(st, &tmA, lead_full, kb * 128, tm * Cfg::kRows + row0, pol_a);
-            load_weight_box_pair(st + Cfg::kABytes, &tmB, lead_full, cr == 0 ? nb0 : nb1, kb, KB, p.b_tiled, pol_b);
+            if constexpr (FUSED) {
+              // weight rows [gate half cr | up half cr]: 64-row boxes
+              load_weight_half_pair(st + Cfg::kABytes, &tmB, lead_full, nb0, cr, kb, KB, p.b_tiled, pol_b);
+              load_weight_half_pair(st + Cfg::kABytes + 8192, &tmB, lead_full, nb1, cr, kb, KB, p.b_tiled, pol_b);
+            } else {
+              load_weight_box_pair(st + Cfg::kABytes, &tmB, lead_full, cr == 0 ? nb0 : nb1, kb, KB, p.b_tiled,
+                                   pol_b);
+            }
           } else {
             mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
             tma_load_2d(st, &tmA, &full[s], kb * 128, tm * Cfg::kRows, pol_a);
-            load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
-            load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
+            if constexpr (FUSED) {
+              // weight rows [gate 0-63 | up 0-63 | gate 64-127 | up 64-127]: 64-row boxes
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                load_weight_half(st + Cfg::kABytes + 16384 * h, &tmB, &full[s], nb0, h, kb, KB, p.b_tiled, pol_b);
+                load_weight_half(st + Cfg::kABytes + 16384 * h + 8192, &tmB, &full[s], nb1, h, kb, KB, p.b_tiled,
+                                 pol_b);
+              }
+            } else {
+              load_weight_box(st + Cfg::kABytes, &tmB, &full[s], nb0, kb, KB, p.b_tiled, pol_b);
+              load_weight_box(st + Cfg::kABytes + 16384, &tmB, &full[s], nb1, kb, KB, p.b_tiled, pol_b);
+            }
           }
           issued |= 1u << s;
           parity_bits = (parity_bits & ~(1u << s)) | (ph << s);
@@ -307,7 +343,11 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     regs_increase<Cfg::Regs::kConsumer>();
     grid_dep_wait();
     // ------------------------------------------------------------ promotion + epilogue
-    const int wg = warp >> 2;         // 0: columns 0-127 of the tile, 1: columns 128-255
+    // Plain: warpgroup wg owns TMEM columns 128wg..+127, i.e. weight block 2tn + wg, one scale per K block.
+    // Fused: the MMA's 256 columns are [gate 0-63 | up 0-63 | gate 64-127 | up 64-127] of gate block tn and
+    // up block tn + I/128, so warpgroup wg holds gate and up of the same 64 output columns 64wg..64wg+63
+    // (accumulator pairs 0-31 gate, 32-63 up) and SiLU(g)*u needs no exchange: two scales per K block.
+    const int wg = warp >> 2;
     const int q = warp & 3;           // TMEM lane quarter
     const int r = q * 32 + lane;      // row inside the tile
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
@@ -323,30 +363,20 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
       prefill_tile_coords(tile, num_m, num_n, p.group_m, p.group_n, tm, tn);
       const int row = tm * Cfg::kRows + row0 + r;
       const bool row_ok = row < M;
-      const int nb = FUSED ? (wg == 0 ? tn : tn + I_blk) : 2 * tn + wg;
+      // plain: this warpgroup's weight block; fused: the gate block (the up block is I_blk further)
+      const int nb = FUSED ? tn : 2 * tn + wg;
       const bool col_ok = nb < nblk;
       const float* as_row = p.As + static_cast<size_t>(row_ok ? row : 0) * KB;
       const float* bs_row = p.Bs + static_cast<size_t>(col_ok ? nb : 0) * KB;
+      const float* bu_row = p.Bs + static_cast<size_t>(FUSED ? nb + I_blk : 0) * KB;
 
       uint64_t acc[64];  // column pairs (2i, 2i+1) of this thread's 128 columns
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0;
 
-      // Scales are prefetched two K blocks ahead through a pair of registers. Rows past M and
-      // the missing half of an odd last column tile read row 0 / block 0: their A rows and weight
-      // rows are zero-filled by TMA, so the partial they scale is zero.
-      float a_n0 = ldg_f32(as_row), b_n0 = ldg_f32(bs_row);
-      float a_n1 = ldg_f32(as_row + (KB > 1 ? 1 : 0)), b_n1 = ldg_f32(bs_row + (KB > 1 ? 1 : 0));
-      for (int kb = 0; kb < KB; ++kb) {
-        const float sa = a_n0, sb = b_n0;
-        a_n0 = a_n1;
-        b_n0 = b_n1;
-        if (kb + 2 < KB) {
-          a_n1 = ldg_f32(as_row + kb + 2);
-          b_n1 = ldg_f32(bs_row + kb + 2);
-        }
-        const float sc = __fmul_rn(sa, sb);
-        const uint64_t sc2 = pack_f2(sc, sc);
+      // One K block: wait for its partial, fold it into the accumulators with the scale products sc2 (the
+      // first 64 columns) and scu2 (the last 64), and hand the TMEM buffer back as soon as it is in registers.
+      auto promote = [&](uint64_t sc2, uint64_t scu2) {
         if (ok && !mbar_wait(&pfull[b], pph, abort_flag, p.status, kErrTimeoutPFull)) ok = false;
         if (ok) {
           tc_fence_after();
@@ -371,11 +401,65 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
             }
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], sc2);
+          for (int i = 0; i < 32; ++i) ffma2(acc[32 + i], v[2 * i], v[2 * i + 1], scu2);
         }
         if (++b == 2) {
           b = 0;
           pph ^= 1;
+        }
+      };
+
+      // Rows past M and the missing half of an odd last column tile read row 0 / block 0: their A rows and
+      // weight rows are zero-filled by TMA, so the partial they scale is zero.
+      if constexpr (FUSED) {
+        // Scales in groups of four K blocks, one group ahead: the loads for K blocks kb0+4 .. kb0+7 are issued
+        // when the group kb0 .. kb0+3 starts and handed over when it ends, so a load has four K blocks to land.
+        // (Refilling each register right after reading it, with no hand-over, measured 20% slower.)
+        constexpr int D = 4;
+        float sa[D], sg[D], su[D];
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+          const int k = j < KB ? j : KB - 1;
+          sa[j] = ldg_f32(as_row + k);
+          sg[j] = ldg_f32(bs_row + k);
+          su[j] = ldg_f32(bu_row + k);
+        }
+        for (int kb0 = 0; kb0 < KB; kb0 += D) {
+          float na[D], ng[D], nu[D];
+#pragma unroll
+          for (int j = 0; j < D; ++j) {
+            const int kn = kb0 + D + j < KB ? kb0 + D + j : KB - 1;
+            na[j] = ldg_f32(as_row + kn);
+            ng[j] = ldg_f32(bs_row + kn);
+            nu[j] = ldg_f32(bu_row + kn);
+          }
+#pragma unroll
+          for (int j = 0; j < D; ++j) {
+            if (kb0 + j >= KB) break;
+            const float scg = __fmul_rn(sa[j], sg[j]), scu = __fmul_rn(sa[j], su[j]);
+            promote(pack_f2(scg, scg), pack_f2(scu, scu));
+          }
+#pragma unroll
+          for (int j = 0; j < D; ++j) {
+            sa[j] = na[j];
+            sg[j] = ng[j];
+            su[j] = nu[j];
+          }
+        }
+      } else {
+        // Scales two K blocks ahead through a pair of registers (the deeper grouping above spills here).
+        float a_n0 = ldg_f32(as_row), b_n0 = ldg_f32(bs_row);
+        float a_n1 = ldg_f32(as_row + (KB > 1 ? 1 : 0)), b_n1 = ldg_f32(bs_row + (KB > 1 ? 1 : 0));
+        for (int kb = 0; kb < KB; ++kb) {
+          const float sa = a_n0, sb = b_n0;
+          a_n0 = a_n1;
+          b_n0 = b_n1;
+          if (kb + 2 < KB) {
+            a_n1 = ldg_f32(as_row + kb + 2);
+            b_n1 = ldg_f32(bs_row + kb + 2);
+          }
+          const float sc = __fmul_rn(sa, sb);
+          promote(pack_f2(sc, sc), pack_f2(sc, sc));
         }
       }
 
@@ -432,73 +516,41 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
           }
         }
       } else {
-        // The 128-wide quant group of row r is split between the two warpgroups: the gate
-        // thread finishes columns 0-63 and the up thread columns 64-127. Each hands the other
-        // the half it lacks through shared memory (the up thread its u[0:64), the gate thread its
-        // g[64:128)), and the two agree on the group's amax through amax_x. 16-byte chunks are
-        // XOR-swizzled by row so the 8 rows of one store phase hit 8 different bank groups; the
-        // swizzle keeps chunks 0-15 (u half) and 16-31 (g half) apart.
-        float4* x4 = reinterpret_cast<float4*>(xch);
-        float* amax_x = xch + 128 * 128;
-        // Accumulator indices must be compile-time constants (a runtime index would move the
-        // whole array to local memory), so each warpgroup runs its own instance of the steps.
-        auto finish_half = [&](auto is_up) {
-          constexpr bool kUp = decltype(is_up)::value;
-          constexpr int give = kUp ? 0 : 32;   // first pair handed to the other warpgroup
-          constexpr int keep = kUp ? 32 : 0;   // first pair finished here
-          constexpr int c4_give = kUp ? 0 : 16;
-          constexpr int c4_take = kUp ? 16 : 0;
+        // y = silu(g) * u for this thread's 64 columns (64wg .. 64wg+63 of the quant group), in place of the
+        // gate accumulators; the 128-wide group's amax is the max of the two warpgroups' halves, met through
+        // amax_x. scale = max(amax, 1e-10) / 448, inv = 1 / scale, q = sat_e4m3(y * inv) (H:532-579).
+        float* amax_x = xch;  // [128 rows][2 halves]
+        float amax = 0.f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int c4 = c4_give + j;
-            x4[r * 32 + (c4 ^ (r & 7))] = make_float4(lo_f(acc[give + 2 * j]), hi_f(acc[give + 2 * j]),
-                                                      lo_f(acc[give + 2 * j + 1]), hi_f(acc[give + 2 * j + 1]));
-          }
-          named_bar_sync(1, 256);
-          float amax = 0.f;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int c4 = c4_take + j;
-            const float4 o = x4[r * 32 + (c4 ^ (r & 7))];
-            const int e = keep + 2 * j;
-            const float a0 = lo_f(acc[e]), a1 = hi_f(acc[e]), a2 = lo_f(acc[e + 1]), a3 = hi_f(acc[e + 1]);
-            // gate thread: g = own, u = other; up thread: g = other, u = own
-            const float y0 = kUp ? silu_mul(o.x, a0) : silu_mul(a0, o.x);
-            const float y1 = kUp ? silu_mul(o.y, a1) : silu_mul(a1, o.y);
-            const float y2 = kUp ? silu_mul(o.z, a2) : silu_mul(a2, o.z);
-            const float y3 = kUp ? silu_mul(o.w, a3) : silu_mul(a3, o.w);
-            acc[e] = pack_f2(y0, y1);
-            acc[e + 1] = pack_f2(y2, y3);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
-          }
-          amax_x[r * 2 + (kUp ? 1 : 0)] = amax;
-          named_bar_sync(1, 256);
-          amax = fmaxf(amax_x[r * 2], amax_x[r * 2 + 1]);
-          const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
-          const float inv = __fdiv_rn(1.0f, scale);
-          if (ok && row_ok) {
-            const int I = I_blk * 128;
-            if (!kUp) p.qs[static_cast<size_t>(row) * I_blk + tn] = scale;
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * I +
-                                                  static_cast<size_t>(tn) * 128 + (kUp ? 64 : 0));
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t w[4];
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const int e = keep + 8 * j + 2 * h;  // pair index: columns 16j + 4h .. +3 of this half
-                w[h] = f2_to_e4m3x2(__fmul_rn(lo_f(acc[e]), inv), __fmul_rn(hi_f(acc[e]), inv)) |
-                       (f2_to_e4m3x2(__fmul_rn(lo_f(acc[e + 1]), inv), __fmul_rn(hi_f(acc[e + 1]), inv)) << 16);
-              }
-              dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-        };
-        if (wg == 0)
-          finish_half(std::false_type{});
-        else
-          finish_half(std::true_type{});
+        for (int i = 0; i < 32; ++i) {
+          const float y0 = silu_mul(lo_f(acc[i]), lo_f(acc[32 + i]));
+          const float y1 = silu_mul(hi_f(acc[i]), hi_f(acc[32 + i]));
+          acc[i] = pack_f2(y0, y1);
+          amax = fmaxf(amax, fmaxf(fabsf(y0), fabsf(y1)));
+        }
+        amax_x[r * 2 + wg] = amax;
         named_bar_sync(1, 256);
+        amax = fmaxf(amax_x[r * 2], amax_x[r * 2 + 1]);
+        const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
+        const float inv = __fdiv_rn(1.0f, scale);
+        if (ok && row_ok) {
+          const int I = I_blk * 128;
+          if (wg == 0) p.qs[static_cast<size_t>(row) * I_blk + tn] = scale;
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * I +
+                                                static_cast<size_t>(tn) * 128 + wg * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const int e = 8 * j + 2 * h;  // pairs e, e+1: columns 16j + 4h .. +3 of this half
+              w[h] = f2_to_e4m3x2(__fmul_rn(lo_f(acc[e]), inv), __fmul_rn(hi_f(acc[e]), inv)) |
+                     (f2_to_e4m3x2(__fmul_rn(lo_f(acc[e + 1]), inv), __fmul_rn(hi_f(acc[e + 1]), inv)) << 16);
+            }
+            dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        named_bar_sync(1, 256);  // amax_x is free for the next tile
       }
       BS_TR_ADD(3);
     }

@@ -7,14 +7,28 @@ namespace bs {
 
 constexpr int kQuantThreads = 256;
 
+// Correctly rounded fp32 quotient x / s from r = RN(1/s): q0 = RN(x * r), e = x - s * q0 (exact in one
+// fma), q = RN(q0 + e * r). This is Markstein's correction step (P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; the quotient theorem in
+// Muller et al., Handbook of Floating-Point Arithmetic, ch. 4): with r the correctly rounded reciprocal and
+// q0 within one ulp of x / s, the remainder e is exact and q is RN(x / s), as long as no intermediate is
+// subnormal. Here s >= 1e-12 and the only quotients that reach e4m3 above zero satisfy |x| >= 2^-10 * s,
+// so the e4m3 byte always equals that of the IEEE quotient; the sign is copied from x so that x = -0
+// gives -0. One reciprocal per 128-group replaces 128 IEEE divisions.
+__device__ __forceinline__ float div_by_scale(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-s, q0, x);
+  return copysignf(__fmaf_rn(e, r, q0), x);
+}
+
 // x bf16 [M, K] -> A e4m3 [M, K], As fp32 [M, K/128].
 // Sixteen threads own one 128-wide group (8 elements = one 16-byte load each), reduce |x| with
 // shuffles inside the half-warp, then
 //     As = max(amax / 448, 1e-12),  A = e4m3_rn(x / As)
 // which is the reference's torch quantiser (scripts/fp8_gemm_factor_check.py:22-27:
 // `s = amax / FP8_MAX; s = s.clamp_min(1e-12); (x / s).to(float8_e4m3fn)`), computed in fp32
-// with IEEE division so the bytes match it exactly. |x / As| <= 448 * (1 + 2^-23), which
-// rounds to 448 under both torch's conversion and the saturating cvt used here.
+// with correctly rounded division (div_by_scale) so the bytes match it exactly. |x / As| <= 448 * (1 + 2^-23),
+// which rounds to 448 under both torch's conversion and the saturating cvt used here.
 __global__ void __launch_bounds__(kQuantThreads)
     k_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, uint8_t* __restrict__ A, float* __restrict__ As,
                   int M, int K) {
@@ -52,20 +66,21 @@ __global__ void __launch_bounds__(kQuantThreads)
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
+    const float rs = __frcp_rn(s);
     if (active) {
       uint2 q;
-      q.x = f2_to_e4m3x2(__fdiv_rn(v[0], s), __fdiv_rn(v[1], s)) |
-            (f2_to_e4m3x2(__fdiv_rn(v[2], s), __fdiv_rn(v[3], s)) << 16);
-      q.y = f2_to_e4m3x2(__fdiv_rn(v[4], s), __fdiv_rn(v[5], s)) |
-            (f2_to_e4m3x2(__fdiv_rn(v[6], s), __fdiv_rn(v[7], s)) << 16);
+      q.x = f2_to_e4m3x2(div_by_scale(v[0], s, rs), div_by_scale(v[1], s, rs)) |
+            (f2_to_e4m3x2(div_by_scale(v[2], s, rs), div_by_scale(v[3], s, rs)) << 16);
+      q.y = f2_to_e4m3x2(div_by_scale(v[4], s, rs), div_by_scale(v[5], s, rs)) |
+            (f2_to_e4m3x2(div_by_scale(v[6], s, rs), div_by_scale(v[7], s, rs)) << 16);
       *reinterpret_cast<uint2*>(A + row * K + kb * 128 + sub * 8) = q;
       if (sub == 0) As[row * KB + kb] = s;
     }
   }
 }
 
-constexpr int kNormThreads = 256;  // one CTA per row
-constexpr int kNormMaxRounds = 8;  // K <= 256 threads x 8 elements x 8 rounds = 16384
+constexpr int kNormThreads = 256;  // eight warps per CTA
+constexpr int kNormMaxK = 16384;
 
 __device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float (&v)[8]) {
   const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -76,107 +91,171 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float (&v)[8]) {
     v[2 * i + 1] = f.y;
   }
 }
-__device__ __forceinline__ float bf16_rn(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// RMSNorm followed by the per-token-group quant, one 256-thread CTA per row, without storing the bf16
-// norm output. The rounding points are those of the unfused pair "RMSNorm -> per_token_group_quant_fp8":
-//   h   = x                                   (or bf16_rn(x + residual), written back to residual)
-//   ss  = sum of h*h in fp32 (no fused multiply-add) in a fixed order that depends on K only: thread t
-//         adds the squares of its elements 8(t + 256j) + e in (j, e) order, each warp combines its lanes
-//         in a butterfly (xor 16, 8, 4, 2, 1), then ss = ((w0 + w1) + w2) + ... + w7 over the 8 warps
-//   rs  = 1 / sqrt(ss / K + eps)                (IEEE divide and square root)
-//   y   = bf16_rn((h * rs) * w)                 (the bf16 value an unfused RMSNorm stores)
-//   As  = max(amax(y over 128) / 448, 1e-12),  A = e4m3_rn(y / As)   (as k_group_quant; a 128-group is
-//         the 16 chunks of one half-warp in one round)
-// All of a thread's chunks (at most 8) are loaded before any is used; the second pass reads the row
-// again from L1.
-template <int ROUNDS>  // chunks per thread: K <= 2048 * ROUNDS
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): each lane is one ordinary IEEE operation, rounded to nearest.
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t ffma2r(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// Two bf16 (low half = first element) -> the fp32 pair (exact: a bf16 is the top half of an fp32).
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t v) {
+  return static_cast<uint64_t>(v << 16) | (static_cast<uint64_t>(v & 0xffff0000u) << 32);
+}
+// The fp32 pair rounded to bf16 (nearest even) and widened back: the value an unfused bf16 store keeps.
+__device__ __forceinline__ uint64_t round_bf16_f2(uint64_t v) { return bf16x2_to_f2(pack_bf16x2(lo_f(v), hi_f(v))); }
+// div_by_scale on a pair.
+__device__ __forceinline__ uint64_t div_by_scale2(uint64_t y, uint64_t neg_s, uint64_t r) {
+  const uint64_t q0 = fmul2(y, r);
+  const uint64_t q = ffma2r(ffma2r(neg_s, q0, y), r, q0);
+  const uint64_t sign = 0x8000000080000000ull;
+  return (q & ~sign) | (y & sign);
+}
+
+// Per-token-group quant of a row, optionally after RMSNorm, in one HBM pass. W warps own one row (W a power
+// of two with at most kRowChunks 16-byte chunks per thread: K = 5120 takes four warps, five chunks each); a
+// 256-thread CTA holds 8 / W rows. Thread t of the row's 32W threads holds the chunks c = t + 32W j (j < 8),
+// so each 128-group is the 16 chunks of one half-warp at one j. NORM = false quantises x itself (the
+// activation quant ahead of a linear); NORM = true has the rounding points of the unfused pair
+// "RMSNorm -> per_token_group_quant_fp8":
+//   h   = x                                   (or bf16_rn(x + residual) with RES, written back to residual)
+//   ss  = sum of h*h in fp32 (products rounded, no fused multiply-add) in a fixed order that depends on K only:
+//         thread t keeps two partial sums, of the even and of the odd elements of its chunks, adding
+//         h[8c + 2e]^2 (resp. h[8c + 2e + 1]^2) for its chunks in increasing c and e = 0..3; its total is
+//         even + odd; each warp combines its lanes in a butterfly (xor 16, 8, 4, 2, 1); the row's sum is the
+//         W warp totals added in warp order, ((w0 + w1) + w2) + ...
+//   rs  = 1 / sqrt(ss / K + eps)              (IEEE divide and square root)
+//   y   = bf16_rn((h * rs) * w)               (the bf16 value an unfused RMSNorm stores)
+// and then, in both cases,
+//   As  = max(amax(y over 128) / 448, 1e-12),  A = e4m3_rn(y / As)   (the reference's torch quantiser,
+//         scripts/fp8_gemm_factor_check.py:22-27, with correctly rounded division, div_by_scale)
+// A thread loads all of its chunks before using any; the arithmetic runs on fp32 pairs.
+constexpr int kRowChunks = 8;
+template <int W, bool NORM, bool RES>
 __global__ void __launch_bounds__(kNormThreads)
-    k_rmsnorm_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* residual, int ldr,
-                          const __nv_bfloat16* __restrict__ w, float eps, uint8_t* __restrict__ A,
-                          float* __restrict__ As, int M, int K) {
-  static_assert(ROUNDS >= 1 && ROUNDS <= kNormMaxRounds, "rounds per thread");
+    k_row_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* residual, int ldr,
+                      const __nv_bfloat16* __restrict__ w, float eps, uint8_t* __restrict__ A,
+                      float* __restrict__ As, int M, int K) {
+  static_assert(W == 1 || W == 2 || W == 4 || W == 8, "warps per row");
+  static_assert(NORM || !RES, "the residual add belongs to the norm");
+  constexpr int C = kRowChunks;
   __shared__ float warp_ss[kNormThreads / 32];
   if (threadIdx.x == 0) grid_dep_launch();
   grid_dep_wait();  // x and the residual may be the previous kernel's output
-  const int t = threadIdx.x;
-  const int lane = t & 31;
-  const int row = blockIdx.x;
-  const int nch = K / 8;  // 16-byte chunks in the row
-  const int rounds = (nch + kNormThreads - 1) / kNormThreads;
-  const __nv_bfloat16* xr = x + static_cast<size_t>(row) * ldx;
-  __nv_bfloat16* rr = residual ? residual + static_cast<size_t>(row) * ldr : nullptr;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rloc = warp / W;  // row inside the CTA
+  const int row = blockIdx.x * (kNormThreads / 32 / W) + rloc;
+  const int t = (warp % W) * 32 + lane;
+  const bool row_ok = row < M;
+  const int nch = K / 8;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(row_ok ? row : 0) * ldx;
+  __nv_bfloat16* rr = RES ? residual + static_cast<size_t>(row_ok ? row : 0) * ldr : nullptr;
 
-  uint4 xv[ROUNDS], rv[ROUNDS];
+  uint4 xv[C];
 #pragma unroll
-  for (int j = 0; j < ROUNDS; ++j) {
-    const int c = j * kNormThreads + t;
-    if (j < rounds && c < nch) {
-      xv[j] = __ldg(reinterpret_cast<const uint4*>(xr + c * 8));
-      if (rr) rv[j] = *reinterpret_cast<const uint4*>(rr + c * 8);
-    }
+  for (int j = 0; j < C; ++j) {
+    const int c = t + 32 * W * j;
+    if (row_ok && c < nch) xv[j] = __ldg(reinterpret_cast<const uint4*>(xr + c * 8));
   }
-  float ss = 0.f;
+  if constexpr (RES) {
+    uint4 rv[C];
 #pragma unroll
-  for (int j = 0; j < ROUNDS; ++j) {
-    const int c = j * kNormThreads + t;
-    if (j < rounds && c < nch) {
-      float h[8];
-      unpack_bf16x8(xv[j], h);
-      if (rr) {
-        float r8[8];
-        unpack_bf16x8(rv[j], r8);
-        uint32_t packed[4];
+    for (int j = 0; j < C; ++j) {
+      const int c = t + 32 * W * j;
+      if (row_ok && c < nch) rv[j] = *reinterpret_cast<const uint4*>(rr + c * 8);
+    }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = bf16_rn(__fadd_rn(h[e], r8[e]));
+    for (int j = 0; j < C; ++j) {
+      const int c = t + 32 * W * j;
+      if (row_ok && c < nch) {
+        uint32_t* hw = reinterpret_cast<uint32_t*>(&xv[j]);
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) packed[e] = pack_bf16x2(h[2 * e], h[2 * e + 1]);
-        xv[j] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t h = fadd2(bf16x2_to_f2(hw[e]), bf16x2_to_f2(rw[e]));
+          hw[e] = pack_bf16x2(lo_f(h), hi_f(h));
+        }
         *reinterpret_cast<uint4*>(rr + c * 8) = xv[j];
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(h[e], h[e]));
     }
   }
+  uint64_t rs2 = 0;
+  if constexpr (NORM) {
+    uint64_t ss2 = 0;  // (sum of even elements, sum of odd elements)
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  if (lane == 0) warp_ss[t >> 5] = ss;
-  __syncthreads();
-  ss = warp_ss[0];
+    for (int j = 0; j < C; ++j) {
+      const int c = t + 32 * W * j;
+      if (row_ok && c < nch) {
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
 #pragma unroll
-  for (int i = 1; i < kNormThreads / 32; ++i) ss = __fadd_rn(ss, warp_ss[i]);
-  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t h = bf16x2_to_f2(hw[e]);
+          ss2 = fadd2(ss2, fmul2(h, h));
+        }
+      }
+    }
+    float ss = __fadd_rn(lo_f(ss2), hi_f(ss2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if constexpr (W > 1) {
+      if (lane == 0) warp_ss[warp] = ss;
+      named_bar_sync(1 + rloc, 32 * W);  // the row's warps only
+      ss = warp_ss[rloc * W];
+#pragma unroll
+      for (int i = 1; i < W; ++i) ss = __fadd_rn(ss, warp_ss[rloc * W + i]);
+    }
+    const float rsn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+    rs2 = pack_f2(rsn, rsn);
+  }
 
   const int KB = K / 128;
 #pragma unroll
-  for (int j = 0; j < ROUNDS; ++j) {
-    if (j >= rounds) break;  // uniform across the CTA
-    const int c = j * kNormThreads + t;
-    const bool active = c < nch;
-    float y[8];
-    if (active) {
-      float h[8], wf[8];
-      unpack_bf16x8(xv[j], h);  // h (the residual sum when fused) is still in registers
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(w + c * 8)), wf);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = bf16_rn(__fmul_rn(__fmul_rn(h[e], rs), wf[e]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = 0.f;
-    }
+  for (int j = 0; j < C; ++j) {
+    if (32 * W * j >= nch) break;  // uniform across the CTA
+    const int c = t + 32 * W * j;
+    const bool active = row_ok && c < nch;
+    uint64_t y2[4];
     float amax = 0.f;
+    if (active) {
+      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
+      if constexpr (NORM) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c * 8));
+        const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+        for (int e = 0; e < 4; ++e)
+          y2[e] = round_bf16_f2(fmul2(fmul2(bf16x2_to_f2(hw[e]), rs2), bf16x2_to_f2(ww[e])));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y2[e] = bf16x2_to_f2(hw[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(lo_f(y2[e])), fabsf(hi_f(y2[e]))));
+    }
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float sc = fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
     if (active) {
-      uint2 q;
-      q.x = f2_to_e4m3x2(__fdiv_rn(y[0], sc), __fdiv_rn(y[1], sc)) |
-            (f2_to_e4m3x2(__fdiv_rn(y[2], sc), __fdiv_rn(y[3], sc)) << 16);
-      q.y = f2_to_e4m3x2(__fdiv_rn(y[4], sc), __fdiv_rn(y[5], sc)) |
-            (f2_to_e4m3x2(__fdiv_rn(y[6], sc), __fdiv_rn(y[7], sc)) << 16);
-      *reinterpret_cast<uint2*>(A + static_cast<size_t>(row) * K + c * 8) = q;
+      const float r = __frcp_rn(sc);
+      const uint64_t ns2 = pack_f2(-sc, -sc), r2 = pack_f2(r, r);
+      uint32_t qw[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint64_t q0 = div_by_scale2(y2[2 * h], ns2, r2);
+        const uint64_t q1 = div_by_scale2(y2[2 * h + 1], ns2, r2);
+        qw[h] = f2_to_e4m3x2(lo_f(q0), hi_f(q0)) | (f2_to_e4m3x2(lo_f(q1), hi_f(q1)) << 16);
+      }
+      *reinterpret_cast<uint2*>(A + static_cast<size_t>(row) * K + c * 8) = make_uint2(qw[0], qw[1]);
       if ((lane & 15) == 0) As[static_cast<size_t>(row) * KB + c / 16] = sc;
     }
   }
