@@ -56,12 +56,11 @@ def group_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
     """RMSNorm then the per-token-group quant, with the rounding points of the unfused pair (the bf16 norm
     output, then quant_block) and the library kernel's fixed fp32 summation order for sum(h^2), which
-    depends on K only. A row belongs to W warps (the smallest power of two, at most 8, that leaves each thread
-    at most 8 of the row's K/8 16-byte chunks); thread t of its 32W threads holds the chunks c = t + 32W j and
-    keeps two partial sums, of its even and of its odd elements: for its chunks in increasing c and
-    e = 0..3, even += h[8c + 2e]^2 and odd += h[8c + 2e + 1]^2 (each square rounded, then each add); its
-    total is even + odd; each 32-thread warp combines its threads in a butterfly (xor 16, 8, 4, 2, 1); the
-    row's sum is the W warp totals added in warp order.
+    depends on K only. A row belongs to 256 threads (eight warps); thread t holds the 16-byte chunks
+    c = t + 256 j and keeps two partial sums, of its even and of its odd elements: for its chunks in
+    increasing c and e = 0..3, even += h[8c + 2e]^2 and odd += h[8c + 2e + 1]^2 (each square rounded, then
+    each add); its total is even + odd; each 32-thread warp combines its threads in a butterfly (xor 16, 8, 4,
+    2, 1); the row's sum is the eight warp totals added in warp order.
     rs = 1 / sqrt(ss / K + eps) in IEEE fp32; y = bf16((h * rs) * w).
     With residual: h = bf16(x + residual), which is also returned (the fused add writes it back).
     Returns (A, As, h_bf16 or None)."""
@@ -69,9 +68,7 @@ def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, resid
     h = (xf + residual.float()).to(torch.bfloat16).float() if residual is not None else xf
     M, K = h.shape
     nch = K // 8
-    W = 1
-    while W < 8 and nch > 32 * W * 8:
-        W *= 2
+    W = 8
     T = 32 * W
     hn = h.numpy().astype(np.float32)
     sq = (hn * hn).astype(np.float32)  # fp32 products, rounded once

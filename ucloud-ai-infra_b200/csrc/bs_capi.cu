@@ -509,25 +509,30 @@ __global__ void k_selftest_wait(uint64_t limit_ns, int* status) {
 namespace {
 using RowKernel = void (*)(const __nv_bfloat16*, int, __nv_bfloat16*, int, const __nv_bfloat16*, float, uint8_t*,
                            float*, int, int);
-// Warps per row of k_row_group_quant: the smallest power of two that leaves each thread at most kRowChunks
-// 16-byte chunks (K <= 16384).
-int row_warps(int K) {
-  const int nch = K / 8;
-  int W = 1;
-  while (W < 8 && nch > 32 * W * bs::kRowChunks) W *= 2;
-  return W;
-}
+// k_row_group_quant for K (at most 16384): built for 1..8 chunks of 16 bytes per thread.
 template <bool NORM, bool RES>
-RowKernel row_kernel(int W) {
-  return W == 1 ? bs::k_row_group_quant<1, NORM, RES>
-         : W == 2 ? bs::k_row_group_quant<2, NORM, RES>
-         : W == 4 ? bs::k_row_group_quant<4, NORM, RES>
-                  : bs::k_row_group_quant<8, NORM, RES>;
+RowKernel row_kernel(int K) {
+  const int c = (K / 8 + bs::kNormThreads - 1) / bs::kNormThreads;
+  switch (c) {
+    case 1: return bs::k_row_group_quant<1, NORM, RES>;
+    case 2: return bs::k_row_group_quant<2, NORM, RES>;
+    case 3: return bs::k_row_group_quant<3, NORM, RES>;
+    case 4: return bs::k_row_group_quant<4, NORM, RES>;
+    case 5:
+    case 6: return bs::k_row_group_quant<6, NORM, RES>;
+    default: return bs::k_row_group_quant<8, NORM, RES>;
+  }
 }
-int launch_row_quant(RowKernel kern, int W, const void* x, int ldx, void* residual, int ldr, const void* weight,
+// Persistent row walk: as many CTAs as fit on the SMs at once (at most four per SM), each walking rows
+// gridDim.x apart.
+int launch_row_quant(RowKernel kern, int num_sms, const void* x, int ldx, void* residual, int ldr, const void* weight,
                      float eps, void* A, float* As, int M, int K, void* stream, const char* where) {
-  const int rows_per_cta = bs::kNormThreads / 32 / W;
-  const int grid = (M + rows_per_cta - 1) / rows_per_cta;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, bs::kNormThreads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  cudaGetLastError();
+  if (per_sm > 4) per_sm = 4;
+  const int grid = M < per_sm * num_sms ? M : per_sm * num_sms;
   return launch_pdl(kern, grid, bs::kNormThreads, 0, static_cast<cudaStream_t>(stream), where,
                     static_cast<const __nv_bfloat16*>(x), ldx, static_cast<__nv_bfloat16*>(residual), ldr,
                     static_cast<const __nv_bfloat16*>(weight), eps, static_cast<uint8_t*>(A), As, M, K);
@@ -599,10 +604,9 @@ int bs_fp8_group_quant(const void* x, int ldx, void* A, float* As, int M, int K,
   DeviceState* d = device_state();
   if (!d) return BS_ERR_CUDA;
   if (K <= bs::kNormMaxK) {
-    // rows held whole by one to eight warps: every load of a thread in flight at once
-    const int W = row_warps(K);
-    return launch_row_quant(row_kernel<false, false>(W), W, x, ldx, nullptr, K, nullptr, 0.f, A, As, M, K, stream,
-                            "k_row_group_quant launch");
+    // whole rows per CTA, the next row's loads in flight while the current one is quantised
+    return launch_row_quant(row_kernel<false, false>(K), d->num_sms, x, ldx, nullptr, K, nullptr, 0.f, A, As, M, K,
+                            stream, "k_row_group_quant launch");
   }
   // wider rows: sixteen threads per 128-group, grid-stride over the groups
   const long long groups = static_cast<long long>(M) * (K / 128);
@@ -624,10 +628,10 @@ int bs_fp8_rmsnorm_group_quant(const void* x, int ldx, void* residual, int ldr, 
   if (!x || !weight || !A || !As) return BS_ERR_ARG;
   if (!aligned16(x) || !aligned16(weight) || !aligned16(A) || (residual && !aligned16(residual))) return BS_ERR_ALIGN;
   if (K > bs::kNormMaxK) return BS_ERR_ARG;
-  if (!device_state()) return BS_ERR_CUDA;
-  const int W = row_warps(K);
-  return launch_row_quant(residual ? row_kernel<true, true>(W) : row_kernel<true, false>(W), W, x, ldx, residual,
-                          ldr, weight, eps, A, As, M, K, stream, "k_row_group_quant<norm> launch");
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  return launch_row_quant(residual ? row_kernel<true, true>(K) : row_kernel<true, false>(K), d->num_sms, x, ldx,
+                          residual, ldr, weight, eps, A, As, M, K, stream, "k_row_group_quant<norm> launch");
 }
 
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {

@@ -114,6 +114,14 @@ __device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t v) {
 }
 // The fp32 pair rounded to bf16 (nearest even) and widened back: the value an unfused bf16 store keeps.
 __device__ __forceinline__ uint64_t round_bf16_f2(uint64_t v) { return bf16x2_to_f2(pack_bf16x2(lo_f(v), hi_f(v))); }
+// The group scale max(amax / 448, 1e-12), with amax / 448 correctly rounded by the same correction step
+// from the correctly rounded reciprocal of 448 (a compile-time constant).
+__device__ __forceinline__ float group_scale(float amax) {
+  constexpr float kInv448 = 1.0f / 448.0f;
+  const float q0 = __fmul_rn(amax, kInv448);
+  return fmaxf(__fmaf_rn(__fmaf_rn(-448.0f, q0, amax), kInv448, q0), 1e-12f);
+}
+
 // div_by_scale on a pair.
 __device__ __forceinline__ uint64_t div_by_scale2(uint64_t y, uint64_t neg_s, uint64_t r) {
   const uint64_t q0 = fmul2(y, r);
@@ -122,141 +130,160 @@ __device__ __forceinline__ uint64_t div_by_scale2(uint64_t y, uint64_t neg_s, ui
   return (q & ~sign) | (y & sign);
 }
 
-// Per-token-group quant of a row, optionally after RMSNorm, in one HBM pass. W warps own one row (W a power
-// of two with at most kRowChunks 16-byte chunks per thread: K = 5120 takes four warps, five chunks each); a
-// 256-thread CTA holds 8 / W rows. Thread t of the row's 32W threads holds the chunks c = t + 32W j (j < 8),
-// so each 128-group is the 16 chunks of one half-warp at one j. NORM = false quantises x itself (the
-// activation quant ahead of a linear); NORM = true has the rounding points of the unfused pair
-// "RMSNorm -> per_token_group_quant_fp8":
+// Per-token-group quant of rows, optionally after RMSNorm, in one HBM pass. A CTA of 256 threads owns one row
+// at a time and walks rows blockIdx.x, blockIdx.x + gridDim.x, ...; thread t holds the row's 16-byte chunks
+// c = t + 256 j (j < C), so each 128-group is the 16 chunks of one half-warp at one j. The loads of the next
+// row are issued before the current row is processed, so the HBM stream does not stop for the row's
+// reduction. NORM = false quantises x itself (the activation quant ahead of a linear); NORM = true has the
+// rounding points of the unfused pair "RMSNorm -> per_token_group_quant_fp8":
 //   h   = x                                   (or bf16_rn(x + residual) with RES, written back to residual)
 //   ss  = sum of h*h in fp32 (products rounded, no fused multiply-add) in a fixed order that depends on K only:
 //         thread t keeps two partial sums, of the even and of the odd elements of its chunks, adding
 //         h[8c + 2e]^2 (resp. h[8c + 2e + 1]^2) for its chunks in increasing c and e = 0..3; its total is
 //         even + odd; each warp combines its lanes in a butterfly (xor 16, 8, 4, 2, 1); the row's sum is the
-//         W warp totals added in warp order, ((w0 + w1) + w2) + ...
+//         eight warp totals added in warp order, ((w0 + w1) + w2) + ... + w7
 //   rs  = 1 / sqrt(ss / K + eps)              (IEEE divide and square root)
 //   y   = bf16_rn((h * rs) * w)               (the bf16 value an unfused RMSNorm stores)
 // and then, in both cases,
 //   As  = max(amax(y over 128) / 448, 1e-12),  A = e4m3_rn(y / As)   (the reference's torch quantiser,
 //         scripts/fp8_gemm_factor_check.py:22-27, with correctly rounded division, div_by_scale)
-// A thread loads all of its chunks before using any; the arithmetic runs on fp32 pairs.
-constexpr int kRowChunks = 8;
-template <int W, bool NORM, bool RES>
+// The arithmetic runs on fp32 pairs.
+template <int C, bool NORM, bool RES>
 __global__ void __launch_bounds__(kNormThreads)
     k_row_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* residual, int ldr,
                       const __nv_bfloat16* __restrict__ w, float eps, uint8_t* __restrict__ A,
                       float* __restrict__ As, int M, int K) {
-  static_assert(W == 1 || W == 2 || W == 4 || W == 8, "warps per row");
   static_assert(NORM || !RES, "the residual add belongs to the norm");
-  constexpr int C = kRowChunks;
-  __shared__ float warp_ss[kNormThreads / 32];
+  constexpr int T = kNormThreads;
+  __shared__ float warp_ss[2][T / 32];  // by row parity, so one barrier per row suffices
   if (threadIdx.x == 0) grid_dep_launch();
   grid_dep_wait();  // x and the residual may be the previous kernel's output
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int rloc = warp / W;  // row inside the CTA
-  const int row = blockIdx.x * (kNormThreads / 32 / W) + rloc;
-  const int t = (warp % W) * 32 + lane;
-  const bool row_ok = row < M;
+  const int t = threadIdx.x;
   const int nch = K / 8;
-  const __nv_bfloat16* xr = x + static_cast<size_t>(row_ok ? row : 0) * ldx;
-  __nv_bfloat16* rr = RES ? residual + static_cast<size_t>(row_ok ? row : 0) * ldr : nullptr;
-
-  uint4 xv[C];
-#pragma unroll
-  for (int j = 0; j < C; ++j) {
-    const int c = t + 32 * W * j;
-    if (row_ok && c < nch) xv[j] = __ldg(reinterpret_cast<const uint4*>(xr + c * 8));
-  }
-  if constexpr (RES) {
-    uint4 rv[C];
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      const int c = t + 32 * W * j;
-      if (row_ok && c < nch) rv[j] = *reinterpret_cast<const uint4*>(rr + c * 8);
-    }
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      const int c = t + 32 * W * j;
-      if (row_ok && c < nch) {
-        uint32_t* hw = reinterpret_cast<uint32_t*>(&xv[j]);
-        const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint64_t h = fadd2(bf16x2_to_f2(hw[e]), bf16x2_to_f2(rw[e]));
-          hw[e] = pack_bf16x2(lo_f(h), hi_f(h));
-        }
-        *reinterpret_cast<uint4*>(rr + c * 8) = xv[j];
-      }
-    }
-  }
-  uint64_t rs2 = 0;
-  if constexpr (NORM) {
-    uint64_t ss2 = 0;  // (sum of even elements, sum of odd elements)
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      const int c = t + 32 * W * j;
-      if (row_ok && c < nch) {
-        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint64_t h = bf16x2_to_f2(hw[e]);
-          ss2 = fadd2(ss2, fmul2(h, h));
-        }
-      }
-    }
-    float ss = __fadd_rn(lo_f(ss2), hi_f(ss2));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    if constexpr (W > 1) {
-      if (lane == 0) warp_ss[warp] = ss;
-      named_bar_sync(1 + rloc, 32 * W);  // the row's warps only
-      ss = warp_ss[rloc * W];
-#pragma unroll
-      for (int i = 1; i < W; ++i) ss = __fadd_rn(ss, warp_ss[rloc * W + i]);
-    }
-    const float rsn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
-    rs2 = pack_f2(rsn, rsn);
-  }
-
   const int KB = K / 128;
+
+  auto load_row = [&](int row, uint4 (&xv)[C], uint4 (&rv)[C]) {
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * ldx;
 #pragma unroll
-  for (int j = 0; j < C; ++j) {
-    if (32 * W * j >= nch) break;  // uniform across the CTA
-    const int c = t + 32 * W * j;
-    const bool active = row_ok && c < nch;
-    uint64_t y2[4];
-    float amax = 0.f;
-    if (active) {
-      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
-      if constexpr (NORM) {
+    for (int j = 0; j < C; ++j) {
+      const int c = t + T * j;
+      if (c < nch) xv[j] = __ldg(reinterpret_cast<const uint4*>(xr + c * 8));
+    }
+    if constexpr (RES) {
+      const __nv_bfloat16* rr = residual + static_cast<size_t>(row) * ldr;
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        const int c = t + T * j;
+        if (c < nch) rv[j] = *reinterpret_cast<const uint4*>(rr + c * 8);
+      }
+    }
+  };
+
+  // the norm weight's chunks of this thread, widened once for every row the CTA walks
+  uint64_t wf[NORM ? C : 1][4];
+  if constexpr (NORM) {
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      const int c = t + T * j;
+      if (c < nch) {
         const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c * 8));
         const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          y2[e] = round_bf16_f2(fmul2(fmul2(bf16x2_to_f2(hw[e]), rs2), bf16x2_to_f2(ww[e])));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) y2[e] = bf16x2_to_f2(hw[e]);
+        for (int e = 0; e < 4; ++e) wf[j][e] = bf16x2_to_f2(ww[e]);
       }
+    }
+  }
+  uint4 xv[C], rv[C], xn[C], rn[C];
+  int row = blockIdx.x;
+  if (row < M) load_row(row, xv, rv);
+  for (int parity = 0; row < M; row += gridDim.x, parity ^= 1) {
+    const int next = row + gridDim.x;
+    if (next < M) load_row(next, xn, rn);
+    if constexpr (RES) {
+      __nv_bfloat16* rr = residual + static_cast<size_t>(row) * ldr;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(lo_f(y2[e])), fabsf(hi_f(y2[e]))));
+      for (int j = 0; j < C; ++j) {
+        const int c = t + T * j;
+        if (c < nch) {
+          uint32_t* hw = reinterpret_cast<uint32_t*>(&xv[j]);
+          const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint64_t h = fadd2(bf16x2_to_f2(hw[e]), bf16x2_to_f2(rw[e]));
+            hw[e] = pack_bf16x2(lo_f(h), hi_f(h));
+          }
+          *reinterpret_cast<uint4*>(rr + c * 8) = xv[j];
+        }
+      }
+    }
+    uint64_t rs2 = 0;
+    if constexpr (NORM) {
+      uint64_t ss2 = 0;  // (sum of even elements, sum of odd elements)
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        const int c = t + T * j;
+        if (c < nch) {
+          const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint64_t h = bf16x2_to_f2(hw[e]);
+            ss2 = fadd2(ss2, fmul2(h, h));
+          }
+        }
+      }
+      float ss = __fadd_rn(lo_f(ss2), hi_f(ss2));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) warp_ss[parity][warp] = ss;
+      __syncthreads();
+      ss = warp_ss[parity][0];
+#pragma unroll
+      for (int i = 1; i < T / 32; ++i) ss = __fadd_rn(ss, warp_ss[parity][i]);
+      const float rsn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+      rs2 = pack_f2(rsn, rsn);
     }
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float sc = fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
-    if (active) {
-      const float r = __frcp_rn(sc);
-      const uint64_t ns2 = pack_f2(-sc, -sc), r2 = pack_f2(r, r);
-      uint32_t qw[2];
+    for (int j = 0; j < C; ++j) {
+      if (T * j >= nch) break;  // uniform across the CTA
+      const int c = t + T * j;
+      const bool active = c < nch;
+      uint64_t y2[4];
+      float amax = 0.f;
+      if (active) {
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
+        if constexpr (NORM) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint64_t q0 = div_by_scale2(y2[2 * h], ns2, r2);
-        const uint64_t q1 = div_by_scale2(y2[2 * h + 1], ns2, r2);
-        qw[h] = f2_to_e4m3x2(lo_f(q0), hi_f(q0)) | (f2_to_e4m3x2(lo_f(q1), hi_f(q1)) << 16);
+          for (int e = 0; e < 4; ++e) y2[e] = round_bf16_f2(fmul2(fmul2(bf16x2_to_f2(hw[e]), rs2), wf[j][e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y2[e] = bf16x2_to_f2(hw[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(lo_f(y2[e])), fabsf(hi_f(y2[e]))));
       }
-      *reinterpret_cast<uint2*>(A + static_cast<size_t>(row) * K + c * 8) = make_uint2(qw[0], qw[1]);
-      if ((lane & 15) == 0) As[static_cast<size_t>(row) * KB + c / 16] = sc;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = group_scale(amax);
+      if (active) {
+        const float r = __frcp_rn(sc);
+        const uint64_t ns2 = pack_f2(-sc, -sc), r2 = pack_f2(r, r);
+        uint32_t qw[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint64_t q0 = div_by_scale2(y2[2 * h], ns2, r2);
+          const uint64_t q1 = div_by_scale2(y2[2 * h + 1], ns2, r2);
+          qw[h] = f2_to_e4m3x2(lo_f(q0), hi_f(q0)) | (f2_to_e4m3x2(lo_f(q1), hi_f(q1)) << 16);
+        }
+        *reinterpret_cast<uint2*>(A + static_cast<size_t>(row) * K + c * 8) = make_uint2(qw[0], qw[1]);
+        if ((lane & 15) == 0) As[static_cast<size_t>(row) * KB + c / 16] = sc;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      xv[j] = xn[j];
+      if constexpr (RES) rv[j] = rn[j];
     }
   }
 }
