@@ -141,8 +141,8 @@ int bs_fp8_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 #define BS_PLAN_THREADS 4     /* threads per CTA                                                           */
 #define BS_PLAN_GRID 5        /* CTAs launched                                                             */
 #define BS_PLAN_CLUSTER 6     /* CTAs per cluster (2: CTA pairs)                                           */
-#define BS_PLAN_GROUP_M 7     /* prefill raster: M tiles per group (column sweep), 0 when sweeping rows    */
-#define BS_PLAN_GROUP_N 8     /* prefill raster: N tiles per group (row sweep), 0 when sweeping columns    */
+#define BS_PLAN_GROUP_M 7     /* prefill raster: M tiles per group (tiles walk down each weight column)    */
+#define BS_PLAN_RESERVED 8    /* 0                                                                         */
 #define BS_PLAN_TMEM_COLS 9   /* TMEM columns allocated per CTA                                            */
 #define BS_PLAN_SPLIT 10      /* decode: 0 one CTA per weight tile, s > 0 equal K splits, -1 stream-K      */
 #define BS_PLAN_WARPGROUPS 11 /* promotion warpgroups                                                      */

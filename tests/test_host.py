@@ -145,14 +145,12 @@ def test_select_tiles(lib):
     p = select(34816, 129)
     assert p["kind"] == "prefill" and (p["BM"], p["BN"]) == (128, 256) and p["cluster"] == 1
     f = select(34816, 8192, fused=True)  # CTA pairs from 1024 rows, every M tile in one raster group
-    assert (f["BM"], f["cluster"], f["group_m"], f["group_n"], f["tiles"]) == (256, 2, 32, 0, 32 * 136)
+    assert (f["BM"], f["cluster"], f["group_m"], f["tiles"]) == (256, 2, 32, 32 * 136)
     assert f["grid"] == 2 * min(sms // 2, f["tiles"]) and f["stages"] == 6 and f["tmem_cols"] == 512
-    dn = select(5120, 8192, K=17408)  # activation panel 142.6 MB > L2, weights 89 MB fit: sweep rows
-    assert (dn["group_m"], dn["group_n"], dn["BM"]) == (0, 20, 128)
-    big = select(248320, 8192, K=5120)  # activation panel fits in L2: sweep columns
-    assert big["group_m"] == 64 and big["group_n"] == 0
-    both = select(32768, 8192, K=17408)  # neither fits: groups of 2048 rows
-    assert both["group_m"] == 16 and both["group_n"] == 0
+    dn = select(5120, 8192, K=17408)  # activation panel 142.6 MB > L2: groups of 2048 rows
+    assert (dn["group_m"], dn["BM"]) == (16, 128)
+    big = select(248320, 8192, K=5120)  # activation panel fits in L2: one group
+    assert big["group_m"] == 64
     with pytest.raises(RuntimeError):
         select(34816 + 128, 8192, fused=True)  # fused N2 must be a multiple of 256
 

@@ -39,8 +39,7 @@ struct GemmParams {
   int ldc;           // plain: row stride of the output, in elements
   int b_tiled;       // 1: weights in tile-first layout [N/128][K/128][128][128]; 0: row-major [N, K]
   int out_f32;       // plain: write fp32 instead of bf16
-  int group_m;       // prefill raster: M tiles per group (column sweep), or
-  int group_n;       // when > 0: N tiles per group (row sweep; group_m unused)
+  int group_m;       // prefill raster: M tiles per group
   const float* As;   // [M, KB] activation group scales
   const float* Bs;   // [N/128, KB] weight block scales
   void* out;         // plain: C [M, ldc]; fused: Q e4m3 [M, I]
@@ -68,24 +67,11 @@ struct PrefillCfg {
   static constexpr int kRows = PAIR ? 256 : 128;  // output rows per tile
 };
 
-// Tile index -> (m tile, n tile), grouped so that CTAs running together share A and B tiles in L2.
-// Column sweep (group_n == 0): groups of group_m M tiles; inside a group consecutive tiles walk down one
-// weight column tile, so with every M tile in one group each weight tile is fetched from HBM once while the
-// activation panel stays in L2. Row sweep (group_n > 0): groups of group_n N tiles; inside a group
-// consecutive tiles walk along one activation row block, so each activation tile is fetched once while the
-// group's weight panel stays in L2 (for activation panels larger than L2 whose weights fit).
-__device__ __forceinline__ void prefill_tile_coords(int tile, int num_m, int num_n, int group_m, int group_n,
-                                                    int& tm, int& tn) {
-  if (group_n > 0) {
-    const int per_group = group_n * num_m;
-    const int g = tile / per_group;
-    const int first_n = g * group_n;
-    const int gn = min(num_n - first_n, group_n);
-    const int in = tile - g * per_group;
-    tn = first_n + in % gn;
-    tm = in / gn;
-    return;
-  }
+// Tile index -> (m tile, n tile), grouped so that CTAs running together share A and B tiles in L2: groups of
+// group_m M tiles, and inside a group consecutive tiles walk down one weight column tile, so the group's
+// activation rows stay in L2 while the weight tiles stream past them (with every M tile in one group, each
+// weight tile is fetched from HBM once).
+__device__ __forceinline__ void prefill_tile_coords(int tile, int num_m, int num_n, int group_m, int& tm, int& tn) {
   const int per_group = group_m * num_n;
   const int g = tile / per_group;
   const int first_m = g * group_m;
@@ -209,16 +195,16 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
       grid_dep_wait();  // A and the output may belong to the previous kernel on the stream
-      // The operand that stays in L2 for the whole sweep is kept there; the one streamed once is not.
-      const uint64_t pol_a = p.group_n > 0 ? policy_evict_first() : policy_evict_last();
-      const uint64_t pol_b = p.group_n > 0 ? policy_evict_last() : policy_evict_normal();
+      // The activation rows of a group are kept in L2 while the weight tiles pass.
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
       int s = 0;
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
       BS_TR_DECL(1);
       for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
         int tm, tn;
-        prefill_tile_coords(tile, num_m, num_n, p.group_m, p.group_n, tm, tn);
+        prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
         const int nb0 = FUSED ? tn : 2 * tn;
         const int nb1 = FUSED ? tn + I_blk : 2 * tn + 1;
         for (int kb = 0; kb < KB; ++kb) {
@@ -360,7 +346,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     BS_TR_DECL(4);
     for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int tm, tn;
-      prefill_tile_coords(tile, num_m, num_n, p.group_m, p.group_n, tm, tn);
+      prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
       const int row = tm * Cfg::kRows + row0 + r;
       const bool row_ok = row < M;
       // plain: this warpgroup's weight block; fused: the gate block (the up block is I_blk further)

@@ -138,7 +138,7 @@ def reset_workspaces() -> None:
         buf.zero_()
 
 
-PLAN_FIELDS = ("kind", "tile_rows", "tile_cols", "stages", "threads", "grid", "cluster", "group_m", "group_n",
+PLAN_FIELDS = ("kind", "tile_rows", "tile_cols", "stages", "threads", "grid", "cluster", "group_m", "reserved",
                "tmem_cols", "split", "warpgroups", "smem_bytes", "tiles")  # include/bs_fp8.h BS_PLAN_*
 
 

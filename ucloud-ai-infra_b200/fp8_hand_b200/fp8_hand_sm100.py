@@ -53,7 +53,7 @@ def select(N: int, M: int, K: int = 5120, fused: bool = False) -> dict:
       NTP        decode: tokens padded to a multiple of 16
       stages, threads, grid, cluster, tmem_cols, smem_bytes, warpgroups (promotion)
       split      decode: "tile" (one CTA per weight tile), "k<s>" (s equal K splits) or "stream-k"
-      group_m / group_n   prefill raster: M tiles per group (column sweep) / N tiles per group (row sweep)
+      group_m    prefill raster: M tiles per group (the group's activation rows stay in L2)
     """
     p = _native.launch_plan(M, N, K, fused)
     out = dict(BK=BK, stages=p["stages"], threads=p["threads"], grid=p["grid"], cluster=p["cluster"],
@@ -62,8 +62,7 @@ def select(N: int, M: int, K: int = 5120, fused: bool = False) -> dict:
         split = {0: "tile", -1: "stream-k"}.get(p["split"], f"k{p['split']}")
         out.update(kind="decode", BM=p["tile_rows"], BN=p["tile_cols"], NTP=p["tile_cols"], split=split)
     else:
-        out.update(kind="prefill", BM=p["tile_rows"], BN=p["tile_cols"], group_m=p["group_m"],
-                   group_n=p["group_n"], tiles=p["tiles"])
+        out.update(kind="prefill", BM=p["tile_rows"], BN=p["tile_cols"], group_m=p["group_m"], tiles=p["tiles"])
     return out
 
 
