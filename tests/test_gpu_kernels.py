@@ -198,6 +198,8 @@ GEMM_CASES = [
     (7, 384, 1024),
     (16, 1024, 5120),
     (33, 2048, 1024),
+    (40, 1152, 1024),     # odd number of weight tiles
+    (96, 768, 17408),     # few tiles, each split over many CTAs
     (5, 384, 17408),      # every tile spread over ~50 CTAs (many middle contributors)
     (3, 128, 256),        # fewer units than SMs
     (112, 1024, 5120),
@@ -244,7 +246,7 @@ def test_decode_workspace_reuse_across_shapes(cuda_lib):
             assert O.max_rel_error(C.cpu(), ref) <= GEMM_MAX_REL, (M, N, K)
 
 
-@pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (300, 768, 2048), (128, 256, 17408)])
+@pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (48, 768, 2048), (300, 768, 2048), (128, 256, 17408)])
 def test_gemm_fp32_out_matches_oracle_tightly(cuda_lib, M, N, K):
     A, B, As, Bs, _ = O.make_gemm_case(M, N, K, seed=N + K + M)
     C = _ops().gemm(*_dev(A, B, As, Bs), out_dtype=torch.float32)
