@@ -8,10 +8,12 @@ gate_up (N2 = 2 x 17408) + SiLU*up + per-token-group quant -> down_proj (K = 174
 [8192, 5120], through the drop-in API (GatedMLP with relayouted weights; the SGLang call sites are stood in by
 fp8_hand_b200.sglang_compat). With N > 1 the same MLP runs tensor-parallel: gate_up column-parallel, down_proj
 row-parallel, its bf16 partials either added by the down_proj epilogue into every rank's output through
-NVSwitch multicast (--tp-reduce multimem, two ranks only; every rank falls back to NCCL if any rank cannot map
-the multicast buffer) or summed by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped
-with compute, --tp-chunks). The default, auto, takes the multicast path on 2 GPUs and NCCL from 4. Total work is
-fixed, so scaling is "strong".
+NVSwitch multicast (--tp-reduce multimem, two ranks only), or summed after the GEMM by the switch reduction
+kernel (--tp-reduce switch: each rank reads 1/N of the rows reduced by the switch and stores the sums into every
+rank's copy), or by one NCCL all_reduce (--tp-reduce nccl, optionally in row chunks overlapped with compute,
+--tp-chunks). Every rank falls back to NCCL if any rank cannot map the multicast buffers. The default, auto,
+takes the multicast epilogue on 2 GPUs and NCCL from 3 (at 4 ranks NCCL's all_reduce of the 84 MB partials
+measured slightly faster than the switch reduction kernel). Total work is fixed, so scaling is "strong".
 
 Rank 0 prints one JSON line. `value` is whole-job TFLOP/s with inputs resident in HBM; `e2e` repeats the step
 with the input copied from pinned host memory and the output copied back inside the timed region. Timing:
@@ -337,12 +339,15 @@ def build_mlp(rank, world, device, tp_chunks=TP_CHUNKS, tp_reduce="auto"):
     if tp_reduce == "auto" or (tp_reduce == "multimem" and world > 2):
         tp_reduce = "multimem" if world == 2 else "nccl"
     mlp = tp.TensorParallelMLP(shard, chunks=tp_chunks, reduce=tp_reduce, return_buffer=True)
-    if tp_reduce == "multimem":
-        # Set up the multicast output (collective), then agree on the outcome: if any rank could not map it,
+    if tp_reduce in ("multimem", "switch"):
+        # Set up the multicast buffers (collective), then agree on the outcome: if any rank could not map them,
         # every rank uses the NCCL all_reduce, so no rank waits in a collective the others skip.
         ok, why = 1, ""
         try:
-            mlp.multicast_out(M_PREFILL, HIDDEN, device)
+            if tp_reduce == "multimem":
+                mlp.multicast_out(M_PREFILL, HIDDEN, device)
+            else:
+                mlp.switch_buffers(M_PREFILL, HIDDEN, device)
         except Exception as e:  # noqa: BLE001 - any failure to map the buffer selects NCCL on every rank
             ok, why = 0, f"{type(e).__name__}: {e}"
         flag = torch.tensor([ok], dtype=torch.int32, device=device)
@@ -539,6 +544,9 @@ def run_ours(args, rank, world, device) -> dict | None:
                         ((f"; config[4] tensor-parallel tp={world}, bf16 partials added into every rank's "
                           "output by the down_proj epilogue through NVSwitch multicast (multimem.red), no "
                           "separate collective") if reduce_mode == "multimem" else
+                         (f"; config[4] tensor-parallel tp={world}, bf16 partials summed by the switch reduction "
+                          "kernel (each rank multimem.ld_reduce's 1/N of the rows and multimem.st's the sums to "
+                          "every rank), no NCCL call") if reduce_mode == "switch" else
                          (f"; config[4] tensor-parallel tp={world}, bf16 partials + NCCL all_reduce"
                           + (f" in {args.tp_chunks} row chunks overlapped with compute, GEMM grids on "
                              f"{os.environ.get('BS_FP8_SM_LIMIT', 'all')} SMs" if args.tp_chunks > 1 else ""))
@@ -738,10 +746,11 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--tp-chunks", type=int, default=TP_CHUNKS,
                     help="N > 1: row chunks per MLP step whose all_reduce overlaps the next chunk")
-    ap.add_argument("--tp-reduce", choices=("auto", "multimem", "nccl"), default="auto",
+    ap.add_argument("--tp-reduce", choices=("auto", "multimem", "switch", "nccl"), default="auto",
                     help="N > 1: sum the down_proj partials in its epilogue through NVSwitch multicast "
-                         "(two ranks only; falls back to NCCL where the group has no multicast mapping) or with "
-                         "NCCL; auto: multicast on 2 GPUs, NCCL from 4")
+                         "(multimem, two ranks only), with the switch reduction kernel after the GEMM (switch), "
+                         "or with NCCL; every rank falls back to NCCL where the group has no multicast mapping; "
+                         "auto: multimem on 2 GPUs, NCCL from 3")
     ap.add_argument("--ref-rows", type=int, default=M_PREFILL,
                     help="--impl reference: tokens of the M=8192 batch computed per step (default: all)")
     ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm"), default=None,

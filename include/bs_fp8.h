@@ -40,6 +40,7 @@ extern "C" {
 #define BS_ERR_TIMEOUT_PFULL 103    /* device status: bounded wait for an MMA partial ran out   */
 #define BS_ERR_TIMEOUT_PEMPTY 104   /* device status: bounded wait for a TMEM buffer ran out    */
 #define BS_ERR_TIMEOUT_DRAIN 105    /* device status: teardown drain ran out                    */
+#define BS_ERR_TIMEOUT_PEER 106     /* device status: a peer rank did not reach the TP reduce   */
 #define BS_ERR_TIMEOUT_SELFTEST 199 /* device status: the self-test wait ran out (expected)     */
 
 /* Block-scaled FP8 GEMM:  C[m, n] = sum_kb (A[m, kb] . B[n, kb]) * As[m, kb] * Bs[n/128, kb].
@@ -80,6 +81,26 @@ int bs_fp8_gemm_silu_quant(const void* A, const void* B, void* Q, const float* A
 int bs_fp8_gemm_reduce_multicast(const void* A, const void* B, void* C_mc, const float* As, const float* Bs, int M,
                                  int N, int K, int ldc, int b_tiled, void* workspace, size_t workspace_bytes,
                                  void* stream);
+
+/* Tensor-parallel sum of the ranks' bf16 partials, in place, through the NVSwitch (no counterpart in the
+ * reference, which runs TP=1: scripts/run_sglang_48g.sh:117; it replaces the all_reduce after the
+ * row-parallel down_proj). Every rank calls it with the same arguments except `rank`, on its own GPU:
+ *   data_mc   multicast address of a symmetric bf16 buffer of `count` elements (count % 8 == 0) that holds
+ *             this rank's partial in its own copy; on return every copy holds the sum (the same bytes);
+ *   flags     this rank's copy of a symmetric uint32 buffer of bs_fp8_tp_flag_words(world) words, zeroed
+ *             once before the first call; flags_mc its multicast address;
+ *   epoch     1 on the first call and one more on every later call with the same flags (all ranks alike);
+ *   limit_ns  bound on each wait for the peers (0: 4 s); a rank that runs out records
+ *             BS_ERR_TIMEOUT_PEER in the status word (bs_fp8_status) and its peers run out after it.
+ * Rank r reads the r-th 1/world of the buffer reduced by the switch (fp32 accumulation, one bf16 rounding)
+ * and stores the sums into every copy, so each GPU moves about (world-1)/world of the buffer each way. The
+ * launch is stream-ordered after the GEMM that wrote the partial, and returns only after every rank has
+ * finished writing into this rank's copy and reading from it. */
+int bs_fp8_tp_reduce_switch(unsigned long long data_mc, void* flags, unsigned long long flags_mc, long long count,
+                            int rank, int world, unsigned int epoch, unsigned long long limit_ns, void* stream);
+
+/* uint32 words of the flag buffer bs_fp8_tp_reduce_switch needs for `world` ranks (0 for world < 2). */
+long long bs_fp8_tp_flag_words(int world);
 
 /* Allocation-free variant of bs_fp8_gemm, for callers that cannot call cudaMalloc (an engine that
  * reserves all device memory up front, an embedding whose only allocator is its own arena, a

@@ -9,7 +9,9 @@ Oracle: the single-GPU MLP restated on the CPU (the fused front half on the whol
 blockwise down_proj). Each rank's quant groups are exact column slices of the single-GPU ones, so the
 tensor-parallel result differs from it only by the rounding of the partials (bf16: half an ulp of each
 partial before the sum) and the order of the sum: every output is held to max |out - ref| <= 1e-2 max|ref|
-and a norm error <= 4e-3, and every rank's copy must be bit-identical to the others'.
+and a norm error <= 4e-3, and every rank's copy must be bit-identical to the others'. The reductions covered:
+NCCL all_reduce (bf16 and fp32 partials, row chunks), the switch reduction (multimem.ld_reduce + multimem.st,
+any world size) and, at two ranks, the down_proj epilogue's multimem.red.
 """
 import os
 import socket
@@ -67,6 +69,13 @@ def _worker(rank, world, port, q):
                 "fp32": tp.TensorParallelMLP(shard, partial_dtype=torch.float32)(xd),  # fp32 partials
                 "chunked": tp.TensorParallelMLP(shard, chunks=2)(xd),                 # overlapped row chunks
                 "bf16_decode": tp.TensorParallelMLP(shard)(xs)}
+        # the switch reduction (any world size), prefill and decode sizes, two calls each: the second call
+        # reuses the buffers with the next epoch of the flags
+        mlp_sw = tp.TensorParallelMLP(shard, reduce="switch")
+        for tag, inp in (("sw", xd), ("sw_decode", xs)):
+            first = mlp_sw(inp)
+            outs[tag] = mlp_sw(inp)
+            outs[tag + "_repeat_equal"] = torch.tensor(torch.equal(first, outs[tag]))
         mc_err = None
         if world == 2:
             # down_proj fused with the sum through NVSwitch multicast, prefill and decode sizes, two calls each

@@ -1,5 +1,6 @@
 // C-ABI entry points of libbs_fp8_sm100.so: argument checks, TMA descriptor creation, kernel
 // selection and launch. One translation unit so that every kernel can name the status word.
+#include <algorithm>
 #include <mutex>
 #include <utility>
 #include <cstdio>
@@ -12,6 +13,7 @@
 #include "bs_prefill.cuh"
 #include "bs_decode.cuh"
 #include "bs_quant.cuh"
+#include "bs_tp.cuh"
 #include "../../include/bs_fp8.h"
 
 // Library status word: kernels record the first bounded-wait timeout here.
@@ -560,6 +562,30 @@ int bs_fp8_gemm_reduce_multicast(const void* A, const void* B, void* C_mc, const
                                  void* stream) {
   return run_gemm(false, A, B, C_mc, As, Bs, nullptr, M, N, K, ldc, b_tiled, 0, workspace, workspace_bytes, stream,
                   1);
+}
+
+long long bs_fp8_tp_flag_words(int world) {
+  return world < 2 ? 0 : 2ll * bs::kTpMaxCtas * world;
+}
+
+int bs_fp8_tp_reduce_switch(unsigned long long data_mc, void* flags, unsigned long long flags_mc, long long count,
+                            int rank, int world, unsigned int epoch, unsigned long long limit_ns, void* stream) {
+  if (world < 2 || world > 64 || rank < 0 || rank >= world || count < 0 || count % 8) return BS_ERR_ARG;
+  if (!data_mc || !flags || !flags_mc || epoch == 0) return BS_ERR_ARG;
+  if (data_mc % 16 || flags_mc % 4 || !aligned16(flags)) return BS_ERR_ALIGN;
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  const long long nvec = count / 8;
+  const long long per_rank = (nvec + world - 1) / world;
+  // one vector per thread at least; the same on every rank (same GPU type, same arguments)
+  long long g = (per_rank + bs::kTpThreads - 1) / bs::kTpThreads;
+  g = std::min<long long>(g, std::min(d->num_sms, bs::kTpMaxCtas));
+  g = std::max<long long>(g, 1);
+  cudaGetLastError();
+  bs::k_tp_reduce_switch<<<static_cast<int>(g), bs::kTpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      data_mc, static_cast<uint32_t*>(flags), flags_mc, nvec, rank, world, epoch,
+      limit_ns ? limit_ns : bs::kWaitLimitNs, d->status);
+  return launch_status("k_tp_reduce_switch launch");
 }
 
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {

@@ -25,6 +25,7 @@ enum : int {
   kErrTimeoutPFull = 103,    // promotion warps waited too long for an MMA partial
   kErrTimeoutPEmpty = 104,   // MMA issuer waited too long for a free TMEM partial buffer
   kErrTimeoutDrain = 105,    // teardown waited too long for in-flight copies / MMAs
+  kErrTimeoutPeer = 106,     // tensor-parallel reduce: a peer rank's CTA did not arrive in time
   kErrTimeoutSelftest = 199, // the self-test wait ran out, as it is meant to
 };
 

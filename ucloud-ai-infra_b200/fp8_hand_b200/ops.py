@@ -167,6 +167,30 @@ def gemm_reduce_multicast(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs
     return out
 
 
+def tp_reduce_switch(data: torch.Tensor, data_multicast: int, flags: torch.Tensor, flags_multicast: int, rank: int,
+                     world: int, epoch: int, limit_ns: int = 0) -> torch.Tensor:
+    """In-place tensor-parallel sum of the ranks' bf16 partials through the NVSwitch. `data` is this rank's copy
+    of a symmetric bf16 buffer (contiguous, holding its partial) and `data_multicast` the multicast address of
+    data's first element; `flags` this rank's copy of a symmetric int32 buffer of flag_words(world) words zeroed
+    before the first call, `flags_multicast` its multicast address. Every rank calls with the same epoch (1, 2,
+    ... per call on these flags). On return every rank's `data` holds the same sums."""
+    dev = _cuda(data, flags)
+    _need(data.dtype == torch.bfloat16 and data.is_contiguous(), "data must be contiguous bf16")
+    _need(flags.dtype == torch.int32 and flags.numel() >= tp_flag_words(world), "flags too small for this world")
+    _need(data.numel() % 8 == 0, "data must hold a multiple of 8 elements")
+    lib = _native.lib()
+    with _native.device_guard(dev):
+        _native.check(lib.bs_fp8_tp_reduce_switch(
+            data_multicast, flags.data_ptr(), flags_multicast, data.numel(), rank, world, epoch, limit_ns,
+            _native.stream_handle(dev)), "bs_fp8_tp_reduce_switch")
+    return data
+
+
+def tp_flag_words(world: int) -> int:
+    """int32 words of the flag buffer tp_reduce_switch needs for `world` ranks."""
+    return int(_native.lib().bs_fp8_tp_flag_words(world))
+
+
 def gemm_silu_quant(A: torch.Tensor, B: torch.Tensor, As: torch.Tensor, Bs: torch.Tensor, *,
                     b_tiled: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """gate_up GEMM + SiLU(gate)*up + per-token-group quant: B holds [gate; up] (2I rows).

@@ -23,6 +23,13 @@ B200-side extension the north star asks for:
            Two ranks only: the switch adds the ranks' bf16 partials into each copy in no fixed order, which
            for two partials (0 + a + b) always rounds the same way, but for three or more can round
            differently in different ranks' copies and leave the replicas unequal.
+           reduce="switch": any number of ranks. Each rank's down_proj writes its partial into its own copy of
+           a symmetric buffer (plain local stores), then one kernel (bs_fp8_tp_reduce_switch) has rank r read
+           the r-th 1/tp of the rows reduced by the switch (multimem.ld_reduce, fp32 accumulation) and store
+           the sums into every copy (multimem.st). Each GPU moves about (tp-1)/tp of the [M, H] buffer each way
+           whatever tp is, against (tp-1) x the buffer into every GPU for "multimem"; the kernel's own
+           cross-rank flags order the GEMMs before the reads and the stores before the return, so no NCCL call
+           and no zeroing is needed, and every rank's copy holds the same bytes.
 
 The per-rank math goes through `compute`, an object with group_quant / gemm_silu_quant / gemm:
 the CUDA ops module by default. Tests on CPU ranks pass another implementation to check the
@@ -91,14 +98,15 @@ class TensorParallelMLP:
 
     def __init__(self, shard: MLPShard, group=None, partial_dtype: torch.dtype = torch.bfloat16, compute=None,
                  chunks: int = 1, reduce: str = "nccl", return_buffer: bool = False):
-        """reduce="multimem" returns a copy of the shared output buffer unless return_buffer=True, in which case
-        the caller gets the buffer's row view itself and must consume it before the next call overwrites it."""
+        """reduce="multimem" and reduce="switch" return a copy of the shared output buffer unless
+        return_buffer=True, in which case the caller gets the buffer's row view itself and must consume it before
+        the next call overwrites it."""
         if compute is None:
             from . import ops as compute
-        if reduce not in ("nccl", "multimem"):
-            raise ValueError(f"reduce must be 'nccl' or 'multimem', not {reduce!r}")
-        if reduce == "multimem" and partial_dtype != torch.bfloat16:
-            raise ValueError("the multicast reduction adds bf16 partials")
+        if reduce not in ("nccl", "multimem", "switch"):
+            raise ValueError(f"reduce must be 'nccl', 'multimem' or 'switch', not {reduce!r}")
+        if reduce in ("multimem", "switch") and partial_dtype != torch.bfloat16:
+            raise ValueError("the switch reductions add bf16 partials")
         self.shard = shard
         self.group = group
         self.partial_dtype = partial_dtype
@@ -108,9 +116,12 @@ class TensorParallelMLP:
         if reduce == "multimem" and self.world > 2:
             raise ValueError("reduce='multimem' needs exactly two ranks: with three or more the switch's bf16 "
                              "additions can round differently in different ranks' copies")
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.reduce = reduce if self.world > 1 else "nccl"
         self.return_buffer = return_buffer
         self._mc = None  # (output buffer [rows, n], symmetric-memory handle, multicast address of row 0)
+        self._sw = None  # (data [rows, n], handle, data multicast address, flags, handle, flags multicast address)
+        self._epoch = 0
         self._flag = None
 
     def _sync(self, device) -> None:
@@ -139,6 +150,32 @@ class TensorParallelMLP:
         out, handle, mc = self._mc
         return out[:m], handle, mc
 
+    def switch_buffers(self, m: int, n: int, device) -> tuple:
+        """Rows [0, m) of this rank's copy of the symmetric bf16 partial/output buffer, its multicast address,
+        and the flag buffer with its multicast address, for reduce="switch". Allocated collectively (every rank
+        calls with the same m) on first use and when a larger m arrives, then at least doubling; the flags are
+        zeroed and every rank has zeroed them before any rank's first reduction."""
+        buf = self._sw
+        if buf is None or m > buf[0].shape[0] or n != buf[0].shape[1]:
+            import torch.distributed._symmetric_memory as symm_mem
+            group = self.group if self.group is not None else dist.group.WORLD
+            rows = m if buf is None or n != buf[0].shape[1] else max(m, 2 * buf[0].shape[0])
+            self._sw = None
+            data = symm_mem.empty(rows, n, dtype=torch.bfloat16, device=device)
+            dh = symm_mem.rendezvous(data, group)
+            flags = symm_mem.empty(self.compute.tp_flag_words(self.world), dtype=torch.int32, device=device)
+            flags.zero_()
+            fh = symm_mem.rendezvous(flags, group)
+            if not dh.multicast_ptr or not fh.multicast_ptr:
+                raise RuntimeError("the group has no NVSwitch multicast mapping (NVLS)")
+            torch.cuda.synchronize(device)
+            dist.barrier(group=group)
+            self._sw = (data, dh, dh.multicast_ptr + (data.data_ptr() - dh.buffer_ptrs[dh.rank]),
+                        flags, fh, fh.multicast_ptr + (flags.data_ptr() - fh.buffer_ptrs[fh.rank]))
+            self._epoch = 0
+        data, _, mc, flags, _, fmc = self._sw
+        return data[:m], mc, flags, fmc
+
     def partial(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's [M, H] contribution (before the reduction)."""
         c, s = self.compute, self.shard
@@ -152,6 +189,16 @@ class TensorParallelMLP:
         return [(r, min(r + step, m)) for r in range(0, m, step)]
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.reduce == "switch":
+            c, s = self.compute, self.shard
+            data, mc, flags, fmc = self.switch_buffers(x.shape[0], s.down.shape[0] * (BLOCK if s.tiled else 1),
+                                                       x.device)
+            A, As = c.group_quant(x)
+            Q, Qs = c.gemm_silu_quant(A, s.gate_up, As, s.gate_up_scale, b_tiled=s.tiled)
+            c.gemm(Q, s.down, Qs, s.down_scale, b_tiled=s.tiled, out=data)
+            self._epoch += 1
+            c.tp_reduce_switch(data, mc, flags, fmc, self.rank, self.world, self._epoch)
+            return data if self.return_buffer else data.clone()
         if self.reduce == "multimem":
             c, s = self.compute, self.shard
             out, _, mc = self.multicast_out(x.shape[0], s.down.shape[0] * (BLOCK if s.tiled else 1), x.device)
