@@ -112,8 +112,6 @@ __device__ __forceinline__ uint64_t ffma2r(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t v) {
   return static_cast<uint64_t>(v << 16) | (static_cast<uint64_t>(v & 0xffff0000u) << 32);
 }
-// The fp32 pair rounded to bf16 (nearest even) and widened back: the value an unfused bf16 store keeps.
-__device__ __forceinline__ uint64_t round_bf16_f2(uint64_t v) { return bf16x2_to_f2(pack_bf16x2(lo_f(v), hi_f(v))); }
 // The group scale max(amax / 448, 1e-12), with amax / 448 correctly rounded by the same correction step
 // from the correctly rounded reciprocal of 448 (a compile-time constant).
 __device__ __forceinline__ float group_scale(float amax) {
@@ -122,12 +120,21 @@ __device__ __forceinline__ float group_scale(float amax) {
   return fmaxf(__fmaf_rn(__fmaf_rn(-448.0f, q0, amax), kInv448, q0), 1e-12f);
 }
 
-// div_by_scale on a pair.
-__device__ __forceinline__ uint64_t div_by_scale2(uint64_t y, uint64_t neg_s, uint64_t r) {
-  const uint64_t q0 = fmul2(y, r);
-  const uint64_t q = ffma2r(ffma2r(neg_s, q0, y), r, q0);
-  const uint64_t sign = 0x8000000080000000ull;
-  return (q & ~sign) | (y & sign);
+// -div_by_scale(y, s, r) on a pair, from neg_r = -r: nq0 = RN(y * -r) = -RN(y * r); e = RN(y + s * nq0), the
+// same value and sign as div_by_scale's e; nq = RN(e * -r + nq0), whose addends are the negations of
+// div_by_scale's. So nq = -div_by_scale(y) bit for bit, signed zeros included (y = -0 gives nq = +0): the
+// e4m3 byte of the quotient is the byte of nq with its sign bit flipped, and no copysign is needed.
+__device__ __forceinline__ uint64_t neg_div_by_scale2(uint64_t y, uint64_t s, uint64_t neg_r) {
+  const uint64_t nq0 = fmul2(y, neg_r);
+  return ffma2r(ffma2r(s, nq0, y), neg_r, nq0);
+}
+
+// Per half: max(|a|, |b|) of two packed bf16 pairs (the result's sign bits are the xor of the inputs' and are
+// ignored by the caller). Exact: a comparison, no rounding.
+__device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 // Per-token-group quant of rows, optionally after RMSNorm, in one HBM pass. A CTA of 256 threads owns one row
@@ -148,8 +155,13 @@ __device__ __forceinline__ uint64_t div_by_scale2(uint64_t y, uint64_t neg_s, ui
 //   As  = max(amax(y over 128) / 448, 1e-12),  A = e4m3_rn(y / As)   (the reference's torch quantiser,
 //         scripts/fp8_gemm_factor_check.py:22-27, with correctly rounded division, div_by_scale)
 // The arithmetic runs on fp32 pairs.
+// CTAs per SM the register budget is sized for, per form (measured: the plain quant streams fastest at four,
+// RMSNorm at three, RMSNorm with the residual at two).
+template <bool NORM, bool RES>
+constexpr int kRowMinCtas = NORM ? (RES ? 2 : 3) : 4;
+
 template <int C, bool NORM, bool RES>
-__global__ void __launch_bounds__(kNormThreads)
+__global__ void __launch_bounds__(kNormThreads, kRowMinCtas<NORM, RES>)
     k_row_group_quant(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* residual, int ldr,
                       const __nv_bfloat16* __restrict__ w, float eps, uint8_t* __restrict__ A,
                       float* __restrict__ As, int M, int K) {
@@ -249,32 +261,34 @@ __global__ void __launch_bounds__(kNormThreads)
       if (T * j >= nch) break;  // uniform across the CTA
       const int c = t + T * j;
       const bool active = c < nch;
-      uint64_t y2[4];
+      uint32_t yw[4];  // the bf16 values to quantise, packed in pairs
       float amax = 0.f;
       if (active) {
         const uint32_t* hw = reinterpret_cast<const uint32_t*>(&xv[j]);
-        if constexpr (NORM) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) y2[e] = round_bf16_f2(fmul2(fmul2(bf16x2_to_f2(hw[e]), rs2), wf[j][e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) y2[e] = bf16x2_to_f2(hw[e]);
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (NORM) {
+            const uint64_t v = fmul2(fmul2(bf16x2_to_f2(hw[e]), rs2), wf[j][e]);
+            yw[e] = pack_bf16x2(lo_f(v), hi_f(v));
+          } else {
+            yw[e] = hw[e];
+          }
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(lo_f(y2[e])), fabsf(hi_f(y2[e]))));
+        const uint32_t m = bf16x2_absmax(bf16x2_absmax(yw[0], yw[1]), bf16x2_absmax(yw[2], yw[3]));
+        amax = fmaxf(fabsf(__uint_as_float(m << 16)), fabsf(__uint_as_float(m & 0xffff0000u)));
       }
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float sc = group_scale(amax);
       if (active) {
-        const float r = __frcp_rn(sc);
-        const uint64_t ns2 = pack_f2(-sc, -sc), r2 = pack_f2(r, r);
+        const float nr = -__frcp_rn(sc);
+        const uint64_t s2 = pack_f2(sc, sc), nr2 = pack_f2(nr, nr);
         uint32_t qw[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const uint64_t q0 = div_by_scale2(y2[2 * h], ns2, r2);
-          const uint64_t q1 = div_by_scale2(y2[2 * h + 1], ns2, r2);
-          qw[h] = f2_to_e4m3x2(lo_f(q0), hi_f(q0)) | (f2_to_e4m3x2(lo_f(q1), hi_f(q1)) << 16);
+          const uint64_t q0 = neg_div_by_scale2(bf16x2_to_f2(yw[2 * h]), s2, nr2);
+          const uint64_t q1 = neg_div_by_scale2(bf16x2_to_f2(yw[2 * h + 1]), s2, nr2);
+          qw[h] = (f2_to_e4m3x2(lo_f(q0), hi_f(q0)) | (f2_to_e4m3x2(lo_f(q1), hi_f(q1)) << 16)) ^ 0x80808080u;
         }
         *reinterpret_cast<uint2*>(A + static_cast<size_t>(row) * K + c * 8) = make_uint2(qw[0], qw[1]);
         if ((lane & 15) == 0) As[static_cast<size_t>(row) * KB + c / 16] = sc;
