@@ -764,6 +764,43 @@ def run_kernel_case(args) -> dict:
             "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 3)}
 
 
+def run_tp_reduce_case(args, rank, world, device) -> dict | None:
+    """--kernel tpreduce under torchrun (N >= 2): the switch reduction kernel alone on [M, 5120] bf16 partials
+    against NCCL's all_reduce of the same tensor (NCCL's default algorithm), `iters` calls each after `warmup`,
+    CUDA events, max over ranks."""
+    from fp8_hand_b200 import ops, tp
+    mlp = tp.TensorParallelMLP(None, reduce="switch")
+    data, mc, flags, fmc = mlp.switch_buffers(args.M, HIDDEN, device)
+    g = torch.Generator(device=device).manual_seed(rank)
+    data.copy_(torch.randn(args.M, HIDDEN, device=device, generator=g).to(torch.bfloat16))
+    nc = data.clone()
+
+    def switch():
+        mlp._epoch += 1
+        ops.tp_reduce_switch(data, mc, flags, fmc, rank, world, mlp._epoch)
+
+    out = {}
+    for name, fn in (("switch", switch), ("nccl", lambda: dist.all_reduce(nc))):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        e1.synchronize()
+        out[name] = max_over_ranks(e0.elapsed_time(e1) / args.iters * 1e3, world, device)
+    nbytes = args.M * HIDDEN * 2
+    if rank != 0:
+        return None
+    return {"kernel": "tpreduce", "M": args.M, "N": HIDDEN, "world": world, "bytes": nbytes,
+            "switch_us": round(out["switch"], 1), "nccl_us": round(out["nccl"], 1),
+            "switch_GB/s_each_way": round(nbytes * (1 + 1 / world) / (out["switch"] * 1e-6) / 1e9, 1),
+            "nccl_busbw_GB/s": round(nbytes * 2 * (world - 1) / world / (out["nccl"] * 1e-6) / 1e9, 1)}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -780,14 +817,33 @@ def main() -> int:
                          "auto: multimem on 2 GPUs, NCCL from 3")
     ap.add_argument("--ref-rows", type=int, default=M_PREFILL,
                     help="--impl reference: tokens of the M=8192 batch computed per step (default: all)")
-    ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm"), default=None,
-                    help="run one kernel case alone (--M/--N/--K/--iters/--warmup)")
+    ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm", "tpreduce"), default=None,
+                    help="run one kernel case alone (--M/--N/--K/--iters/--warmup); tpreduce: the switch "
+                         "reduction against NCCL's all_reduce under torchrun")
     ap.add_argument("--M", type=int, default=2048)
     ap.add_argument("--N", type=int, default=2 * INTER)
     ap.add_argument("--K", type=int, default=HIDDEN)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--row-major", dest="tiled", action="store_false", help="--kernel: row-major weights")
     args = ap.parse_args()
+    if args.kernel == "tpreduce":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world < 2:
+            print(json.dumps({"kernel": "tpreduce", "unavailable": "needs torchrun with two or more ranks"}))
+            return 0
+        rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+        device = torch.device("cuda", local)
+        torch.cuda.set_device(device)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        try:
+            res = run_tp_reduce_case(args, rank, world, device)
+            if res is not None:
+                print(json.dumps(res), flush=True)
+        finally:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if args.kernel is not None:
         print(json.dumps(run_kernel_case(args)), flush=True)
         return 0
