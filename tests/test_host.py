@@ -70,6 +70,19 @@ def test_argument_validation_needs_no_gpu(lib):
     assert lib.bs_fp8_rmsnorm_group_quant(None, 17408, None, 17408, None, 1e-6, None, None, 4, 17408, s) == 1
     # null pointers with a real shape
     assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
+    # the switch reduction: at least two ranks, rank in range, a whole number of 16-byte vectors, both multicast
+    # addresses and the flags, a nonzero epoch; then 16-byte / 4-byte alignment
+    ok_args = dict(data_mc=1 << 20, flags=1 << 20, flags_mc=1 << 21, count=8, rank=0, world=2, epoch=1)
+
+    def switch(**kw):
+        a = {**ok_args, **kw}
+        return lib.bs_fp8_tp_reduce_switch(a["data_mc"], a["flags"], a["flags_mc"], a["count"], a["rank"],
+                                           a["world"], a["epoch"], 0, s)
+    assert switch(world=1) == 1 and switch(rank=2) == 1 and switch(rank=-1) == 1 and switch(count=12) == 1
+    assert switch(data_mc=0) == 1 and switch(flags=None) == 1 and switch(flags_mc=0) == 1 and switch(epoch=0) == 1
+    assert switch(data_mc=(1 << 20) + 8) == 2 and switch(flags_mc=(1 << 21) + 2) == 2
+    assert switch(flags=(1 << 20) + 4) == 2
+    assert lib.bs_fp8_tp_flag_words(1) == 0 and lib.bs_fp8_tp_flag_words(8) == 2 * 256 * 8
     # the multicast-reduction GEMM: the same shape rules (bf16 output only), M == 0 a no-op
     assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 0, 256, 256, 256, 0, None, 0, s) == 0
     assert lib.bs_fp8_gemm_reduce_multicast(None, None, None, None, None, 4, 256, 200, 256, 0, None, 0, s) == 1
