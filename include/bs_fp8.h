@@ -54,7 +54,11 @@ extern "C" {
  * M <= 128 runs the swap-AB split-K decode kernel and needs `workspace` of at least
  * bs_fp8_workspace_bytes(M, N, K, 0) bytes, zero-filled before its first use. Its first 64 KB are
  * per-tile arrival counters (at most 16384 weight tiles, N <= 2097152), which every call leaves at
- * zero, so one workspace serves any sequence of shapes on its stream. M > 128 needs no workspace.
+ * zero, so one workspace serves any sequence of shapes on its stream. M > 128 needs no workspace; given
+ * one of bs_fp8_workspace_bytes(M, N, K, 0) bytes (nonzero only for plain prefill shapes whose whole tiles
+ * would fill the last wave of SMs poorly and whose K has 32+ blocks), those shapes run stream-K: every CTA
+ * takes an equal range of (tile, K block) units and tiles shared by two CTAs are summed in a fixed order
+ * through the workspace, under the same zeroed-counter rule.
  * M == 0 is a no-op. */
 int bs_fp8_gemm(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N, int K,
                 int ldc, int b_tiled, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
@@ -115,8 +119,10 @@ long long bs_fp8_tp_flag_words(int world);
 int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N,
                         int K, int ldc, int b_tiled, int out_dtype, void* stream);
 
-/* Workspace bytes the decode kernels need for (M, N, K): the 64 KB counter prefix plus the partial tiles;
- * 0 when M > 128 or M == 0 (no workspace needed) or when the shape has more than 16384 weight tiles. */
+/* Workspace bytes for (M, N, K): the 64 KB counter prefix plus the partial tiles. Decode shapes (M <= 128):
+ * what the split-K kernel needs (0 when the shape has more than 16384 weight tiles). Prefill shapes: the
+ * stream-K workspace (two 128 x 256 fp32 partial tiles per SM) when the plain GEMM runs stream-K, else 0.
+ * 0 for M == 0. */
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused);
 
 /* Per-token-group activation quant: x bf16 [M, K] (row stride ldx elements, multiple of 8) ->

@@ -203,6 +203,24 @@ def test_down_proj_prefill_config(cuda_lib):
     check_gemm(C, A, B, As, Bs, rows=rows, blocks=spread_blocks(N // 128, 8), label="down_proj M=8192")
 
 
+def test_down_proj_stream_k_config(cuda_lib):
+    """down_proj at M = 1024 (K = 17408, N = 5120): 160 whole tiles would take two waves of the 148 SMs for 1.08
+    waves of work, so the kernel runs stream-K (equal K-block ranges per CTA, a tile shared by two CTAs summed
+    through the workspace). At M = 4096 (640 tiles, 86 % of five waves) it runs whole tiles."""
+    M, K, N = 1024, 17408, 5120
+    ops = _ops()
+    from fp8_hand_b200 import select
+    assert select(N, M, K=K)["split"] == "stream-k" and select(N, 4096, K=K)["split"] == "tile"
+    B, Bs = gpu_weight(N, K, seed=141)
+    _, A, As, out_rows = gpu_activation(M, K, seed=142)
+    C = ops.gemm(A, ops.pack_tiles(B), As, Bs, b_tiled=True)
+    C2 = ops.gemm(A, ops.pack_tiles(B), As, Bs, b_tiled=True)
+    torch.cuda.synchronize()
+    assert torch.equal(C, C2), "stream-K sums partials in a fixed order: two calls give the same bytes"
+    rows = sample_rows(M, tile_rows=128, per_tile=4, extra=out_rows[:8], seed=9)
+    check_gemm(C, A, B, As, Bs, rows=rows, blocks=spread_blocks(N // 128, 10), label=f"down_proj stream-K M={M}")
+
+
 def test_mlp_prefill_chain_config(cuda_lib):
     """The whole MLP at M = 8192 through the drop-in API (group quant -> fused gate_up -> down_proj), the
     bench's workload, on sampled rows: down_proj's input is the fused kernel's own (Q, Qs)."""

@@ -211,6 +211,7 @@ GEMM_CASES = [
     (1024, 1024, 2048),   # 256-row tiles on CTA pairs from here on
     (600, 384, 640),      # last pair tile: peer rows all past M, half-empty last column tile
     (520, 2048, 1024),    # last pair tile: 8 valid rows
+    (1040, 4864, 4096),   # 171 tiles on 148 SMs: stream-K (tiles split between neighbouring CTAs), ragged rows
 ]
 
 

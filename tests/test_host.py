@@ -161,7 +161,11 @@ def test_select_tiles(lib):
     assert (f["BM"], f["cluster"], f["group_m"], f["tiles"]) == (256, 2, 32, 32 * 136)
     assert f["grid"] == 2 * min(sms // 2, f["tiles"]) and f["stages"] == 6 and f["tmem_cols"] == 512
     dn = select(5120, 8192, K=17408)  # activation panel 142.6 MB > L2: groups of 2048 rows
-    assert (dn["group_m"], dn["BM"]) == (16, 128)
+    assert (dn["group_m"], dn["BM"]) == (16, 128) and dn["split"] == "tile"  # 1280 tiles: 8.6 full waves
+    # 160 tiles would leave the second wave 8 % full: stream-K, with a workspace of two partial tiles per CTA
+    assert select(5120, 1024, K=17408)["split"] == "stream-k" and f["split"] == "tile"
+    assert lib.bs_fp8_workspace_bytes(1024, 5120, 17408, 0) == 65536 + sms * 2 * 128 * 256 * 4
+    assert lib.bs_fp8_workspace_bytes(8192, 5120, 17408, 0) == 0 and lib.bs_fp8_workspace_bytes(1024, 34816, 5120, 1) == 0
     big = select(248320, 8192, K=5120)  # activation panel fits in L2: one group
     assert big["group_m"] == 64
     with pytest.raises(RuntimeError):

@@ -315,11 +315,11 @@ int max_pair_clusters(int threads, int smem) {
 
 // Persistent prefill launch. PAIR: clusters of two CTAs on one TPC compute 256-row tiles with
 // cta_group::2 MMAs, one cluster per co-resident SM pair.
-template <bool FUSED, bool PAIR>
+template <bool FUSED, bool PAIR, bool SK = false>
 int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::GemmParams& p, int num_tiles,
                    int num_sms, cudaStream_t s) {
   using Cfg = bs::PrefillCfg<FUSED, PAIR>;
-  constexpr auto kern = bs::k_prefill<FUSED, PAIR>;
+  constexpr auto kern = bs::k_prefill<FUSED, PAIR, SK>;
   const int rc = prepare_kernel<kern>(Cfg::kSmemBytes, Cfg::Regs::kLaunch);
   if (rc != BS_OK) return rc;
   if constexpr (PAIR) {
@@ -336,12 +336,17 @@ int launch_prefill(const CUtensorMap& tmA, const CUtensorMap& tmB, const bs::Gem
 // Tile walk of a prefill GEMM (M > 128): tile shape and raster.
 struct PrefillPlan {
   bool pair;             // 256-row tiles on CTA pairs (cta_group::2)
+  bool stream_k;         // plain, one CTA per tile: equal (tile, K block) ranges per CTA (given a workspace)
   int rows;              // output rows per tile
   int num_m, num_n;      // tiles along M and N
   int group_m;           // M tiles per raster group (see prefill_tile_coords)
 };
 
-PrefillPlan prefill_plan(bool fused, int M, int N, int K) {
+// Stream-K workspace of the plain prefill kernel on G CTAs: the 64 KB counter prefix, then two fp32 partial
+// tiles (128 rows x 256 columns) per CTA.
+size_t prefill_ws_bytes(int G) { return kCounterBytes + static_cast<size_t>(G) * 2 * 128 * 256 * 4; }
+
+PrefillPlan prefill_plan(bool fused, int M, int N, int K, int num_sms) {
   PrefillPlan pl;
   pl.pair = M >= pair_min_rows(fused);
   pl.rows = pl.pair ? 256 : 128;
@@ -353,6 +358,15 @@ PrefillPlan prefill_plan(bool fused, int M, int N, int K) {
   // (weights evict_first), 1.13 GB sweeping rows with the weights kept in L2, all at the same time (the
   // kernel is not DRAM-bound there).
   pl.group_m = static_cast<long long>(M) * K <= (48ll << 20) ? pl.num_m : 2048 / pl.rows;
+  // Stream-K when whole tiles would use less than 60 % of the SM-waves they take (down_proj at M = 1024: 160
+  // tiles on 148 SMs take two full tile times for 1.08 tiles of work per SM) and K is long enough (32+ blocks)
+  // for the partial-tile exchange to pay. Measured: down_proj M = 1024 141 -> 109 us, o_proj M = 1024 57.5 ->
+  // 50.3 us; slower: at 72-86 % of the waves (qkv at M = 1024, down_proj at M = 4096), where stream-K's CTAs
+  // spread over every tile at once instead of sharing panels in L2, and at K = 1024 (19 -> 24 us).
+  const long long tiles = static_cast<long long>(pl.num_m) * pl.num_n;
+  const long long waves = (tiles + num_sms - 1) / num_sms;
+  pl.stream_k = !fused && !pl.pair && K / 128 >= 32 && tiles > num_sms && tiles <= kMaxDecodeTiles &&
+                10 * tiles < 6 * waves * num_sms;
   return pl;
 }
 
@@ -374,6 +388,8 @@ int validate_gemm(bool fused, const void* A, const void* B, const void* out, con
 int run_gemm(bool fused, const void* A, const void* B, void* out, const float* As, const float* Bs, float* qs,
              int M, int N, int K, int ldc, int b_tiled, int out_dtype, void* ws, size_t ws_bytes, void* stream,
              int out_mc = 0) {
+  // (prefill: a workspace is optional; given one of bs_fp8_workspace_bytes' size, shapes whose tiles fill the
+  // last wave poorly run stream-K, else every prefill shape runs whole tiles)
   const int vrc = validate_gemm(fused, A, B, out, As, Bs, qs, M, N, K, ldc, b_tiled, out_dtype);
   if (vrc != BS_OK || M == 0) return vrc;
   DeviceState* d = device_state();
@@ -425,9 +441,14 @@ int run_gemm(bool fused, const void* A, const void* B, void* out, const float* A
   if (make_map(&tmA, A, K, M, K, 128, 128) != BS_OK) return BS_ERR_TMAP;
   // the fused kernel interleaves gate and up weight rows in 64-row halves
   if (fused && make_weight_map(&tmB, B, N, K, b_tiled, 64) != BS_OK) return BS_ERR_TMAP;
-  const PrefillPlan pl = prefill_plan(fused, M, N, K);
+  const PrefillPlan pl = prefill_plan(fused, M, N, K, d->num_sms);
   p.group_m = pl.group_m;
   const int tiles = pl.num_m * pl.num_n;
+  if (pl.stream_k && !out_mc && ws && aligned16(ws) && ws_bytes >= prefill_ws_bytes(d->num_sms)) {
+    p.cnt = static_cast<int*>(ws);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+    return launch_prefill<false, false, true>(tmA, tmB, p, tiles, d->num_sms, s);
+  }
   if (pl.pair)
     return fused ? launch_prefill<true, true>(tmA, tmB, p, tiles, d->num_sms, s)
                  : launch_prefill<false, true>(tmA, tmB, p, tiles, d->num_sms, s);
@@ -589,9 +610,10 @@ int bs_fp8_tp_reduce_switch(unsigned long long data_mc, void* flags, unsigned lo
 }
 
 size_t bs_fp8_workspace_bytes(int M, int N, int K, int fused) {
-  if (M <= 0 || M > 128 || N <= 0 || K <= 0 || K % 128 || N % (fused ? 256 : 128)) return 0;
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 || N % (fused ? 256 : 128)) return 0;
   DeviceState* d = device_state();
   const int sms = d ? d->num_sms : 148;
+  if (M > 128) return prefill_plan(fused != 0, M, N, K, sms).stream_k ? prefill_ws_bytes(sms) : 0;
   const int tiles = fused ? N / 256 : N / 128;
   if (tiles > kMaxDecodeTiles) return 0;
   return decode_ws_bytes(decode_grid(sms, tiles, K / 128), fused ? 2 : 1, ntp_for(M));
@@ -697,9 +719,10 @@ int bs_fp8_launch_plan(int M, int N, int K, int fused, int* plan, int n) {
     plan[BS_PLAN_SMEM] = cfg[4];
     return BS_OK;
   }
-  const PrefillPlan pl = prefill_plan(fused != 0, M, N, K);
+  const PrefillPlan pl = prefill_plan(fused != 0, M, N, K, sms);
   const int tiles = pl.num_m * pl.num_n;
   plan[BS_PLAN_KIND] = 2;
+  plan[BS_PLAN_SPLIT] = pl.stream_k ? -1 : 0;  // stream-K needs the workspace bs_fp8_workspace_bytes reports
   plan[BS_PLAN_TILE_ROWS] = pl.rows;
   plan[BS_PLAN_TILE_COLS] = 256;
   if (pl.pair) {

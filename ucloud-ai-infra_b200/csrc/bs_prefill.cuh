@@ -81,6 +81,34 @@ __device__ __forceinline__ void prefill_tile_coords(int tile, int num_m, int num
   tn = in / gm;
 }
 
+// Segment i (0, 1, ...) of one CTA's work: tile `tile`, K blocks [kb0, kb1). Whole tiles c, c + G, ... without
+// stream-K; with it, the contiguous (tile, K block) units [c*U/G, (c+1)*U/G) of U = num_tiles * KB cut at tile
+// boundaries, so every CTA streams the same number of K blocks and a tile may be shared by neighbouring CTAs.
+// Returns false past the last segment.
+__device__ __forceinline__ bool prefill_segment(int i, int c, int G, int num_tiles, int KB, bool stream_k, int& tile,
+                                                int& kb0, int& kb1) {
+  if (!stream_k) {
+    tile = c + i * G;
+    kb0 = 0;
+    kb1 = KB;
+    return tile < num_tiles;
+  }
+  const long long U = static_cast<long long>(num_tiles) * KB;
+  const long long u0 = U * c / G, u1 = U * (c + 1) / G;
+  const long long us = i == 0 ? u0 : (u0 / KB + i) * KB;
+  if (us >= u1) return false;
+  tile = static_cast<int>(us / KB);
+  kb0 = static_cast<int>(us - static_cast<long long>(tile) * KB);
+  const long long ue = u1 < static_cast<long long>(tile + 1) * KB ? u1 : static_cast<long long>(tile + 1) * KB;
+  kb1 = static_cast<int>(ue - static_cast<long long>(tile) * KB);
+  return true;
+}
+
+// CTA whose stream-K range holds unit u (U units over G CTAs).
+__device__ __forceinline__ int prefill_unit_owner(long long u, long long U, int G) {
+  return static_cast<int>(((u + 1) * G - 1) / U);
+}
+
 // Weight box for (128-row block nb, K block kb) in either supported layout.
 __device__ __forceinline__ void load_weight_box(void* dst, const CUtensorMap* map, uint64_t* bar, int nb, int kb,
                                                 int KB, int tiled, uint64_t policy) {
@@ -122,10 +150,13 @@ __device__ __forceinline__ void prefetch_weight_box(const CUtensorMap* map, int 
     tma_prefetch_l2_2d(map, kb * 128, nb * 128);
 }
 
-template <bool FUSED, bool PAIR>
+// SK (plain, one CTA per tile only): stream-K, CTAs take equal ranges of (tile, K block) units; the partial
+// tiles go through p.ws with per-tile arrival counters in p.cnt.
+template <bool FUSED, bool PAIR, bool SK = false>
 __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const GemmParams p) {
+  static_assert(!SK || (!FUSED && !PAIR), "stream-K runs the plain kernel on single CTAs");
   using Cfg = PrefillCfg<FUSED, PAIR>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -138,6 +169,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
   uint64_t* drain = bars + 2 * S + 4;   // [1] MMA teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // stream-K: this CTA finishes the tile
   float* xch = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes);
 
   const int warp = threadIdx.x >> 5;
@@ -183,6 +215,7 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
   const int num_tiles = num_m * num_n;
   const int tile0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int tstep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  constexpr bool sk = SK;
   const int row0 = PAIR ? static_cast<int>(cr) * 128 : 0;  // this CTA's first row inside a tile
 
   // Each role changes its register budget at the top of its own branch: code after a merge of
@@ -202,12 +235,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
       uint32_t ph = 0, issued = 0, parity_bits = 0;
       bool ok = true;
       BS_TR_DECL(1);
-      for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
+      int tile, kbs, kbe;
+      for (int seg = 0; ok && prefill_segment(seg, tile0, tstep, num_tiles, KB, sk, tile, kbs, kbe); ++seg) {
         int tm, tn;
         prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
         const int nb0 = FUSED ? tn : 2 * tn;
         const int nb1 = FUSED ? tn + I_blk : 2 * tn + 1;
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = kbs; kb < kbe; ++kb) {
           BS_TR_MARK();
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) {
             ok = false;
@@ -275,8 +309,9 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
       uint32_t ph = 0, pph = 0;
       bool ok = true;
       BS_TR_DECL(2);
-      for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
-        for (int kb = 0; kb < KB; ++kb) {
+      int tile, kbs, kbe;
+      for (int seg = 0; ok && prefill_segment(seg, tile0, tstep, num_tiles, KB, sk, tile, kbs, kbe); ++seg) {
+        for (int kb = kbs; kb < kbe; ++kb) {
           BS_TR_MARK();
           if (!mbar_wait(&full[s], ph, abort_flag, p.status, kErrTimeoutFull)) {
             ok = false;
@@ -344,7 +379,8 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
     uint32_t pph = 0;
     bool ok = true;
     BS_TR_DECL(4);
-    for (int tile = tile0; tile < num_tiles; tile += tstep) {
+    int tile, kbs, kbe;
+    for (int seg = 0; prefill_segment(seg, tile0, tstep, num_tiles, KB, sk, tile, kbs, kbe); ++seg) {
       int tm, tn;
       prefill_tile_coords(tile, num_m, num_n, p.group_m, tm, tn);
       const int row = tm * Cfg::kRows + row0 + r;
@@ -434,18 +470,67 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
         }
       } else {
         // Scales two K blocks ahead through a pair of registers (the deeper grouping above spills here).
-        float a_n0 = ldg_f32(as_row), b_n0 = ldg_f32(bs_row);
-        float a_n1 = ldg_f32(as_row + (KB > 1 ? 1 : 0)), b_n1 = ldg_f32(bs_row + (KB > 1 ? 1 : 0));
-        for (int kb = 0; kb < KB; ++kb) {
+        const int kn1 = kbs + 1 < kbe ? kbs + 1 : kbs;
+        float a_n0 = ldg_f32(as_row + kbs), b_n0 = ldg_f32(bs_row + kbs);
+        float a_n1 = ldg_f32(as_row + kn1), b_n1 = ldg_f32(bs_row + kn1);
+        for (int kb = kbs; kb < kbe; ++kb) {
           const float sa = a_n0, sb = b_n0;
           a_n0 = a_n1;
           b_n0 = b_n1;
-          if (kb + 2 < KB) {
+          if (kb + 2 < kbe) {
             a_n1 = ldg_f32(as_row + kb + 2);
             b_n1 = ldg_f32(bs_row + kb + 2);
           }
           const float sc = __fmul_rn(sa, sb);
           promote(pack_f2(sc, sc), pack_f2(sc, sc));
+        }
+      }
+
+      if constexpr (SK) {
+        if (!(kbs == 0 && kbe == KB)) {
+          // Stream-K, a tile shared with other CTAs: store this CTA's partial (fp32, [slot][half][4-column group]
+          // [row] as float4, so a warp's stores are contiguous), count the arrival, and let the last arriver add
+          // every contributor's partial in CTA order and run the epilogue. Nobody waits on another CTA.
+          const long long U = static_cast<long long>(num_tiles) * KB;
+          const long long tu0 = static_cast<long long>(tile) * KB;
+          const int c = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x);
+          const int c_first = prefill_unit_owner(tu0, U, G), c_last = prefill_unit_owner(tu0 + KB - 1, U, G);
+          const long long cu0 = U * c / G;
+          const int my_slot = (c == c_first && cu0 < tu0) ? 1 : 0;
+          float4* part = reinterpret_cast<float4*>(p.ws) + (static_cast<size_t>(c * 2 + my_slot) * 2 + wg) * 4096 + r;
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              part[j * 128] = make_float4(lo_f(acc[2 * j]), hi_f(acc[2 * j]), lo_f(acc[2 * j + 1]),
+                                          hi_f(acc[2 * j + 1]));
+          }
+          // Release: the barrier orders every promotion thread's stores before thread 0's fence and increment.
+          named_bar_sync(1, 256);
+          if (threadIdx.x == 0) {
+            __threadfence();
+            const int prev = atomicAdd(&p.cnt[tile], 1);
+            const int last = prev == c_last - c_first;
+            if (last) p.cnt[tile] = 0;
+            *last_flag = last;
+          }
+          named_bar_sync(1, 256);
+          // (thread 0 rewrites the flag only after the first barrier of a later shared segment, which every
+          // thread reaches after this read)
+          if (*last_flag == 0) continue;
+          __threadfence();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) acc[i] = 0;
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            const int sl = (cc == c_first && U * cc / G < tu0) ? 1 : 0;
+            const float4* src = reinterpret_cast<const float4*>(p.ws) + (static_cast<size_t>(cc * 2 + sl) * 2 + wg) * 4096 + r;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float4 v = __ldcg(src + j * 128);
+              acc[2 * j] = pack_f2(lo_f(acc[2 * j]) + v.x, hi_f(acc[2 * j]) + v.y);
+              acc[2 * j + 1] = pack_f2(lo_f(acc[2 * j + 1]) + v.z, hi_f(acc[2 * j + 1]) + v.w);
+              if ((j & 15) == 15) compiler_fence();  // 16 loads in flight per thread
+            }
+          }
         }
       }
 

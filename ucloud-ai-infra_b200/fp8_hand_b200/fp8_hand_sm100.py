@@ -52,7 +52,9 @@ def select(N: int, M: int, K: int = 5120, fused: bool = False) -> dict:
       BM, BN, BK tile: decode 128 weight rows x NTP tokens; prefill 128 or 256 (CTA pairs) rows x 256 columns
       NTP        decode: tokens padded to a multiple of 16
       stages, threads, grid, cluster, tmem_cols, smem_bytes, warpgroups (promotion)
-      split      decode: "tile" (one CTA per weight tile), "k<s>" (s equal K splits) or "stream-k"
+      split      decode: "tile" (one CTA per weight tile), "k<s>" (s equal K splits) or "stream-k"; prefill:
+                 "tile" (whole output tiles) or "stream-k" (plain GEMMs whose tiles would fill the last wave
+                 less than 90 %; it runs when the call has the workspace bs_fp8_workspace_bytes reports)
       group_m    prefill raster: M tiles per group (the group's activation rows stay in L2)
     """
     p = _native.launch_plan(M, N, K, fused)
@@ -62,7 +64,8 @@ def select(N: int, M: int, K: int = 5120, fused: bool = False) -> dict:
         split = {0: "tile", -1: "stream-k"}.get(p["split"], f"k{p['split']}")
         out.update(kind="decode", BM=p["tile_rows"], BN=p["tile_cols"], NTP=p["tile_cols"], split=split)
     else:
-        out.update(kind="prefill", BM=p["tile_rows"], BN=p["tile_cols"], group_m=p["group_m"], tiles=p["tiles"])
+        out.update(kind="prefill", BM=p["tile_rows"], BN=p["tile_cols"], group_m=p["group_m"], tiles=p["tiles"],
+                   split="stream-k" if p["split"] == -1 else "tile")
     return out
 
 
