@@ -119,6 +119,14 @@ long long bs_fp8_tp_flag_words(int world);
 int bs_fp8_gemm_noalloc(const void* A, const void* B, void* C, const float* As, const float* Bs, int M, int N,
                         int K, int ldc, int b_tiled, int out_dtype, void* stream);
 
+/* The unfused chain's activation between the gate_up GEMM and the activation quant (only when the fused
+ * kernel is off: SGLANG_FP8_HAND_FUSED=0): gate_up bf16 [M, 2I] (row stride ld_in) -> out bf16 [M, I] (row
+ * stride ld_out) with out = bf16(silu(g) * u) in fp32, one rounding, g = gate_up[:, :I], u = gate_up[:, I:].
+ * Replaces SGLang's silu_and_mul in the chain the reference restates at
+ * logs/artifacts/20261031_hand/fused_test.py:30-34 (its fallback for M < 1024, H:678-687). I % 8 == 0,
+ * strides multiples of 8, pointers 16-byte aligned. */
+int bs_fp8_silu_mul(const void* gate_up, int ld_in, void* out, int ld_out, int M, int I, void* stream);
+
 /* Workspace bytes for (M, N, K): the 64 KB counter prefix plus the partial tiles. Decode shapes (M <= 128):
  * what the split-K kernel needs (0 when the shape has more than 16384 weight tiles). Prefill shapes: the
  * stream-K workspace (two 128 x 256 fp32 partial tiles per SM) when the plain GEMM runs stream-K, else 0.

@@ -79,6 +79,29 @@ def test_group_quant_strided_rows(cuda_lib):
     assert torch.equal(A.cpu().view(torch.uint8), qr.view(torch.uint8)) and torch.equal(As.cpu(), sr)
 
 
+@pytest.mark.parametrize("M,inter,strided", [(1, 8, False), (300, 512, False), (37, 17408, True)])
+def test_silu_mul_matches_oracle(cuda_lib, M, inter, strided):
+    """The unfused chain's SiLU(g)*u kernel against the oracle's fp32 expression (torch silu on the CPU, one
+    bf16 rounding). CUDA's expf and the CPU's exp may differ in the last fp32 bit, so at most 0.1 % of the
+    outputs may differ, by one bf16 ulp. Zeros, tiny and large-magnitude gates are among the inputs."""
+    g = torch.Generator().manual_seed(M + inter)
+    gu = (torch.randn(M, 2 * inter, generator=g) * 4).to(torch.bfloat16)
+    gu[0, : min(inter, 8)] = torch.tensor([0.0, -0.0, 80.0, -80.0, 1e-30, -1e-30, 3.0, -3.0])[: min(inter, 8)].to(
+        torch.bfloat16)
+    dev = gu.cuda()
+    if strided:
+        big = torch.zeros(M, 2 * inter + 64, dtype=torch.bfloat16, device="cuda")
+        big[:, : 2 * inter] = dev
+        dev = big[:, : 2 * inter]
+    y = _ops().silu_mul(dev).cpu()
+    ref = (torch.nn.functional.silu(gu[:, :inter].float()) * gu[:, inter:].float()).to(torch.bfloat16)
+    assert y.shape == ref.shape and y.dtype == torch.bfloat16
+    a, b = y.view(torch.int16).int(), ref.view(torch.int16).int()
+    diff = (a - b).abs()
+    assert int(diff.max()) <= 1, int(diff.max())
+    assert (diff > 0).float().mean().item() <= 1e-3
+
+
 @pytest.mark.parametrize("M,K,fused_add", [(1, 128, False), (7, 640, True), (300, 5120, False), (33, 5120, True),
                                             (64, 16384, True), (2049, 1024, True), (2048, 5120, False)])
 def test_rmsnorm_group_quant_bit_exact(cuda_lib, M, K, fused_add):

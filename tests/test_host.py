@@ -70,6 +70,11 @@ def test_argument_validation_needs_no_gpu(lib):
     assert lib.bs_fp8_rmsnorm_group_quant(None, 17408, None, 17408, None, 1e-6, None, None, 4, 17408, s) == 1
     # null pointers with a real shape
     assert lib.bs_fp8_gemm(None, None, None, None, None, 4, 256, 256, 256, 0, 0, None, 0, s) == 1
+    # the unfused chain's SiLU*up: width a multiple of 8, strides covering the rows; M == 0 a no-op
+    assert lib.bs_fp8_silu_mul(None, 16, None, 8, 0, 8, s) == 0
+    assert lib.bs_fp8_silu_mul(None, 24, None, 12, 4, 12, s) == 1
+    assert lib.bs_fp8_silu_mul(None, 8, None, 8, 4, 8, s) == 1
+    assert lib.bs_fp8_silu_mul(None, 16, None, 8, 4, 8, s) == 1  # null pointers with a real shape
     # the switch reduction: at least two ranks, rank in range, a whole number of 16-byte vectors, both multicast
     # addresses and the flags, a nonzero epoch; then 16-byte / 4-byte alignment
     ok_args = dict(data_mc=1 << 20, flags=1 << 20, flags_mc=1 << 21, count=8, rank=0, world=2, epoch=1)

@@ -657,6 +657,21 @@ int bs_fp8_rmsnorm_group_quant(const void* x, int ldx, void* residual, int ldr, 
                           residual, ldr, weight, eps, A, As, M, K, stream, "k_row_group_quant<norm> launch");
 }
 
+int bs_fp8_silu_mul(const void* gate_up, int ld_in, void* out, int ld_out, int M, int I, void* stream) {
+  if (M < 0 || I <= 0 || I % 8 || ld_in < 2 * I || ld_in % 8 || ld_out < I || ld_out % 8) return BS_ERR_ARG;
+  if (M == 0) return BS_OK;
+  if (!gate_up || !out) return BS_ERR_ARG;
+  if (!aligned16(gate_up) || !aligned16(out)) return BS_ERR_ALIGN;
+  DeviceState* d = device_state();
+  if (!d) return BS_ERR_CUDA;
+  const long long chunks = static_cast<long long>(M) * (I / 8);
+  const long long want = (chunks + 255) / 256;
+  const int grid = static_cast<int>(want < 4ll * d->num_sms ? want : 4ll * d->num_sms);
+  return launch_pdl(bs::k_silu_mul, grid, 256, 0, static_cast<cudaStream_t>(stream), "k_silu_mul launch",
+                    static_cast<const __nv_bfloat16*>(gate_up), ld_in, static_cast<__nv_bfloat16*>(out), ld_out, M,
+                    I);
+}
+
 int bs_fp8_pack_tiles(const void* W, void* tiles, int N, int K, void* stream) {
   if (N <= 0 || K <= 0 || N % 128 || K % 128) return BS_ERR_ARG;
   if (!W || !tiles) return BS_ERR_ARG;

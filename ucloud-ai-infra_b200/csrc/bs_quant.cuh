@@ -302,6 +302,38 @@ __global__ void __launch_bounds__(kNormThreads, kRowMinCtas<NORM, RES>)
   }
 }
 
+// The unfused chain's activation (SGLang's silu_and_mul between the gate_up GEMM and the activation quant when
+// the fused kernel is off): y[m, j] = bf16(silu(g) * u) with g = gu[m, j], u = gu[m, I + j], computed in fp32
+// with one rounding at the end, silu(g) = g / (1 + exp(-g)) (IEEE division, CUDA's expf). Eight columns per
+// thread (16-byte loads and stores), grid-stride over the rows' 8-column chunks.
+__global__ void __launch_bounds__(256) k_silu_mul(const __nv_bfloat16* __restrict__ gu, int ld_in,
+                                                  __nv_bfloat16* __restrict__ y, int ld_out, int M, int I) {
+  if (threadIdx.x == 0) grid_dep_launch();
+  grid_dep_wait();  // gu is the previous kernel's output
+  const int per_row = I / 8;
+  const long long total = static_cast<long long>(M) * per_row;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / per_row);
+    const int c = static_cast<int>(i - static_cast<long long>(m) * per_row) * 8;
+    const __nv_bfloat16* row = gu + static_cast<size_t>(m) * ld_in;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(row + c));
+    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(row + I + c));
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&uv);
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint64_t g2 = bf16x2_to_f2(gw[e]), u2 = bf16x2_to_f2(uw[e]);
+      const float g0 = lo_f(g2), g1 = hi_f(g2);
+      const float y0 = __fmul_rn(__fdiv_rn(g0, __fadd_rn(1.0f, expf(-g0))), lo_f(u2));
+      const float y1 = __fmul_rn(__fdiv_rn(g1, __fadd_rn(1.0f, expf(-g1))), hi_f(u2));
+      ow[e] = pack_bf16x2(y0, y1);
+    }
+    *reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * ld_out + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
 // tiles[nb][kb][r][c] = W[nb*128 + r][kb*128 + c]; one CTA per 16 KB tile, 16-byte moves.
 // Byte-for-byte the permute of the reference's relayout (patches/fp8_hand_sm89.py:667).
 __global__ void __launch_bounds__(256) k_pack_tiles(const uint8_t* __restrict__ W, uint8_t* __restrict__ tiles, int N,

@@ -34,6 +34,7 @@ SIGNATURES = {
     "bs_fp8_group_quant": (_I, [_VP, _I, _VP, _VP, _I, _I, _VP]),
     "bs_fp8_rmsnorm_group_quant": (_I, [_VP, _I, _VP, _I, _VP, ctypes.c_float, _VP, _VP, _I, _I, _VP]),
     "bs_fp8_pack_tiles": (_I, [_VP, _VP, _I, _I, _VP]),
+    "bs_fp8_silu_mul": (_I, [_VP, _I, _VP, _I, _I, _I, _VP]),
     "bs_fp8_tp_reduce_switch": (_I, [_U64, _VP, _U64, ctypes.c_longlong, _I, _I, ctypes.c_uint, _U64, _VP]),
     "bs_fp8_tp_flag_words": (ctypes.c_longlong, [_I]),
     "bs_fp8_status": (_I, [ctypes.POINTER(_I), _I]),

@@ -53,6 +53,25 @@ def group_quant(x: torch.Tensor, group_size: int = BLOCK) -> tuple[torch.Tensor,
     return A.view(*x.shape[:-1], K), As.view(*x.shape[:-1], K // BLOCK)
 
 
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """gate_up bf16 [..., 2I] -> bf16 [..., I]: silu(g) * u in fp32 with one rounding (SGLang's silu_and_mul,
+    the unfused chain's activation)."""
+    _need(gate_up.dtype == torch.bfloat16, "gate_up must be bf16")
+    dev = _cuda(gate_up)
+    n2 = gate_up.shape[-1]
+    _need(n2 % 16 == 0, "gate_up width must be a multiple of 16")
+    x2 = gate_up.reshape(-1, n2)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M, inter = x2.shape[0], n2 // 2
+    y = torch.empty((M, inter), dtype=torch.bfloat16, device=dev)
+    with _native.device_guard(dev):
+        _native.check(_native.lib().bs_fp8_silu_mul(
+            x2.data_ptr(), x2.stride(0), y.data_ptr(), inter, M, inter, _native.stream_handle(dev)),
+            "bs_fp8_silu_mul")
+    return y.view(*gate_up.shape[:-1], inter)
+
+
 def rmsnorm_group_quant(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
                         residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """RMSNorm fused with the per-token-group quant of its output (the next linear's activation quant):

@@ -65,10 +65,9 @@ class Fp8BlockLinear(nn.Module):
 
 def silu_and_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """The unfused chain's activation (SGLang silu_and_mul): only reached when the fused kernel is
-    switched off (SGLANG_FP8_HAND_FUSED=0) or ineligible."""
-    inter = gate_up.shape[-1] // 2
-    g, u = gate_up[..., :inter].float(), gate_up[..., inter:].float()
-    return (torch.nn.functional.silu(g) * u).to(gate_up.dtype)
+    switched off (SGLANG_FP8_HAND_FUSED=0) or ineligible. Runs the library's kernel (bs_fp8_silu_mul)."""
+    from . import ops
+    return ops.silu_mul(gate_up)
 
 
 class GatedMLP(nn.Module):
