@@ -729,7 +729,13 @@ def run_kernel_case(args) -> dict:
     torch.cuda.set_device(device)
     M, N, K = args.M, args.N, args.K
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
-    if args.kernel in ("quant", "norm"):
+    if args.kernel == "silu":
+        g = torch.Generator(device=device).manual_seed(3)
+        gu = (torch.randn(M, 2 * K, device=device, generator=g) * 2).to(torch.bfloat16)
+        fn = lambda: ops.silu_mul(gu)  # noqa: E731
+        nbytes = M * 2 * K * 2 + M * K * 2
+        flops = 0.0
+    elif args.kernel in ("quant", "norm"):
         g = torch.Generator(device=device).manual_seed(3)
         x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
         w = torch.ones(K, dtype=torch.bfloat16, device=device)
@@ -817,9 +823,9 @@ def main() -> int:
                          "auto: multimem on 2 GPUs, NCCL from 3")
     ap.add_argument("--ref-rows", type=int, default=M_PREFILL,
                     help="--impl reference: tokens of the M=8192 batch computed per step (default: all)")
-    ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm", "tpreduce"), default=None,
-                    help="run one kernel case alone (--M/--N/--K/--iters/--warmup); tpreduce: the switch "
-                         "reduction against NCCL's all_reduce under torchrun")
+    ap.add_argument("--kernel", choices=("fused", "gemm", "quant", "norm", "silu", "tpreduce"), default=None,
+                    help="run one kernel case alone (--M/--N/--K/--iters/--warmup; silu: [M, 2K] -> [M, K]); "
+                         "tpreduce: the switch reduction against NCCL's all_reduce under torchrun")
     ap.add_argument("--M", type=int, default=2048)
     ap.add_argument("--N", type=int, default=2 * INTER)
     ap.add_argument("--K", type=int, default=HIDDEN)
