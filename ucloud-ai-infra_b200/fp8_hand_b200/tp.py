@@ -1,7 +1,7 @@
 """Tensor-parallel MLP over NCCL: one process per GPU inside one 8 x B200 box.
 
 The reference runs on one GPU (scripts/run_sglang_48g.sh:117, `--tp-size 1`); this is the
-B200-side extension the north star asks for:
+B200-side extension for an 8-GPU box:
 
   gate_up  column-parallel, no collective. Rank r keeps gate rows [r*I/tp, (r+1)*I/tp) and the
            same up rows, packed as [gate_r; up_r], so the fused kernel's "up starts at N2/2"
