@@ -22,7 +22,7 @@
 // As[t,kb]*Bs[nb,kb] into a ring of eight slots in shared memory, so the promotion warps never
 // wait on a global load and never synchronise with each other inside the K loop. Promotion
 // warpgroup g owns the tokens [g*TR, (g+1)*TR) of every weight group (TR = NTP/PWG). Plain: one
-// warpgroup up to 32 tokens, two from 48. Fused: two warpgroups, four (each with gate and up of a
+// warpgroup up to 32 tokens, two at 48..64, four from 80. Fused: two warpgroups, four (each with gate and up of a
 // quarter of the tokens) for 48..80 tokens. setmaxnreg moves registers from the producer
 // warpgroup to the promotion warps (40/232 at 384 threads, 32/112 at 640).
 //
@@ -51,8 +51,10 @@ struct DecodeCfg {
   static_assert(NTP % 16 == 0 && NTP >= 16 && NTP <= 128, "tokens per MMA must be 16..128, step 16");
   static constexpr int kNwg = FUSED ? 2 : 1;               // weight blocks per unit: gate (+ up)
   // Promotion warpgroups. Fused at 96+ tokens: two warpgroups with 232 registers measured faster
-  // than four with 112.
-  static constexpr int kPwg = FUSED ? (NTP >= 48 && NTP <= 80 ? 4 : 2) : (NTP >= 48 ? 2 : 1);
+  // than four with 112. Plain from 80 tokens: four warpgroups (20..32 tokens each) measured 4-8 % faster
+  // than two (down_proj at 72..128 tokens, lm_head at 112 and 128, the config-1 GEMM); at 48..64 tokens
+  // two stay faster.
+  static constexpr int kPwg = FUSED ? (NTP >= 48 && NTP <= 80 ? 4 : 2) : (NTP >= 80 ? 4 : NTP >= 48 ? 2 : 1);
   static constexpr int kTr = NTP / kPwg;                   // tokens per promotion warpgroup
   static_assert(kTr % 4 == 0, "token range must be whole ulonglong2 scale loads");
   static constexpr int kPromo = 128 * kPwg;
