@@ -412,17 +412,16 @@ def run_ours(args, rank, world, device) -> dict | None:
 
     # e2e: every step copies its input from pinned host memory to the device, runs the MLP through
     # the public API and copies the result back to pinned host memory, all inside the timed region.
-    # Copies run on their own streams with two device buffers each way, so step i's upload and
-    # step i-1's download overlap step i's compute (the usual serving pipeline); the timed region
-    # spans from the first upload to the last download.
+    # Copies run on their own streams with two device input buffers, so step i's upload and step i-1's
+    # download overlap step i's compute (the usual serving pipeline); each step's output is downloaded
+    # straight from the tensor the API returns (kept alive, and marked as used by the download stream, until
+    # its copy is done). The timed region spans from the first upload to the last download.
     xh = x.cpu().pin_memory()
     oh = torch.empty(M_PREFILL, HIDDEN, dtype=torch.bfloat16).pin_memory()
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     xd = [torch.empty_like(x) for _ in range(2)]
-    od = [torch.empty(M_PREFILL, HIDDEN, dtype=torch.bfloat16, device=device) for _ in range(2)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
 
     def pipelined(nsteps, e_start=None, e_end=None):
         if e_start is not None:
@@ -435,14 +434,14 @@ def run_ours(args, rank, world, device) -> dict | None:
                 xd[j].copy_(xh, non_blocking=True)
                 ev_in[j].record(s_in)
             stream.wait_event(ev_in[j])
-            if i >= 2:
-                stream.wait_event(ev_out[j])         # download of step i-2 finished with od[j]
-            od[j].copy_(step(xd[j]))
+            out = step(xd[j])
+            if world > 1:
+                out = out.clone()  # the TP MLP hands out its shared output buffer, which the next step rewrites
             ev_done[j].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_done[j])
-                oh.copy_(od[j], non_blocking=True)
-                ev_out[j].record(s_out)
+                out.record_stream(s_out)             # its memory is not reused before this copy ends
+                oh.copy_(out, non_blocking=True)
         if e_end is not None:
             e_end.record(s_out)
 
@@ -455,7 +454,7 @@ def run_ours(args, rank, world, device) -> dict | None:
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
     clk.__exit__(None, None, None)
-    del xd, od
+    del xd
 
     # The MLP at the other prefill sizes (same weights, event-timed median of 5 steps, max over ranks).
     prefill = {}
