@@ -273,7 +273,8 @@ def test_decode_workspace_reuse_across_shapes(cuda_lib):
             assert O.max_rel_error(C.cpu()[rows], ref) <= GEMM_MAX_REL, (M, N, K)
 
 
-@pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (48, 768, 2048), (300, 768, 2048), (128, 256, 17408)])
+@pytest.mark.parametrize("M,N,K", [(9, 768, 2048), (48, 768, 2048), (300, 768, 2048), (128, 256, 17408),
+                                   (1040, 4864, 4096)])  # the last on stream-K
 def test_gemm_fp32_out_matches_oracle_tightly(cuda_lib, M, N, K):
     A, B, As, Bs, _ = O.make_gemm_case(M, N, K, seed=N + K + M)
     C = _ops().gemm(*_dev(A, B, As, Bs), out_dtype=torch.float32)
