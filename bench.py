@@ -213,7 +213,8 @@ def event_ms(fn, warmup=3, reps=5) -> float:
 
 
 def make_graph_timer(device, world, reps=50):
-    """Per-call microseconds of fn (or of fns, cycled) as a CUDA graph of `reps` back-to-back calls: a decode
+    """Per-call microseconds of fn (or of fns, cycled) as a CUDA graph of `reps` back-to-back calls (the median of
+    three replays, max over ranks): a decode
     step is served from a captured graph, and the Python wrapper costs more than the kernel. Passing several
     closures over different weight copies rotates a working set larger than L2 through the graph."""
     stream = torch.cuda.current_stream(device)
@@ -233,13 +234,16 @@ def make_graph_timer(device, world, reps=50):
         g.replay()
         torch.cuda.synchronize()
         barrier(world)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        g.replay()
-        e.record(stream)
-        torch.cuda.synchronize()
+        times = []
+        for _ in range(3):  # the median of three replays
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            g.replay()
+            e.record(stream)
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e) / reps)
         del g
-        return max_over_ranks(s.elapsed_time(e) / reps, world, device) * 1e3
+        return max_over_ranks(statistics.median(times), world, device) * 1e3
 
     return graph_us
 
@@ -531,7 +535,7 @@ def run_ours(args, rank, world, device) -> dict | None:
                          "TFLOP/s": round(mlp_flops(112) / (us * 1e-6) / 1e12, 2),
                          "weight_GB/s_per_rank": round((fused_bytes(112, n2_local) +
                                                         gemm_bytes(112, n_down, k_down)) / (us * 1e-6) / 1e9, 1),
-                         "timing": "CUDA graph of 50 back-to-back MLP steps, collective inside, max over ranks"}
+                         "timing": "CUDA graph of 50 back-to-back MLP steps, collective inside, median of 3 replays, max over ranks"}
         except RuntimeError as e:  # every rank runs the same capture, so every rank lands here alike
             tp_decode = {"M": 112, "unavailable": f"{type(e).__name__}: {e}"[:200]}
 
@@ -594,9 +598,9 @@ def run_ours(args, rank, world, device) -> dict | None:
         },
         "prefill_mlp": {"unit": "TFLOP/s", "timing": "event-timed median of 5 steps", "by_M": prefill},
         "decode_fused_gate_up": {"unit": "GB/s", "hbm_peak_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
-                                 "timing": "CUDA graph of 50 back-to-back calls", "by_M": decode},
+                                 "timing": "CUDA graph of 50 back-to-back calls, median of 3 replays", "by_M": decode},
         "decode_down_proj": {"unit": "GB/s", "hbm_peak_gbs": hbm,
-                             "timing": f"CUDA graph of 50 back-to-back calls over {n_copies} weight copies",
+                             "timing": f"CUDA graph of 50 back-to-back calls over {n_copies} weight copies, median of 3 replays",
                              "by_M": decode_down},
         **({"tp_decode_mlp": tp_decode} if tp_decode else {}),
         "e2e": {"value": round(mlp_flops(M_PREFILL) / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",

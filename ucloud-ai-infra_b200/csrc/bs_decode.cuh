@@ -430,12 +430,13 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
               for (int i = 0; i < TR; ++i)
                 if (tok0 + i < M) part[(w * NTP + tok0 + i) * 128] = pair_elem(acc[w][i / 2], i & 1);
           }
-          // Release: the barrier orders every promotion thread's partial stores before thread 0's
-          // device-scope fence, which makes them visible before the counter increment.
+          // The barrier orders every promotion thread's partial stores before thread 0's counter increment, one
+          // acq_rel atomic at device scope: its release (cumulative through the barrier) publishes the partials,
+          // its acquire orders the finisher's reads below (after the next barrier).
           named_bar_sync(1, NPROMO);
           if (tid == 0) {
-            __threadfence();
-            const int prev = atomicAdd(&p.cnt[t], 1);
+            int prev;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(p.cnt + t) : "memory");
             const int last = prev == c_last - c_first;
             if (last) p.cnt[t] = 0;
             *last_flag = last;
@@ -443,7 +444,6 @@ __global__ void __launch_bounds__(DecodeCfg<FUSED, NTP>::kThreads, 1)
           named_bar_sync(1, NPROMO);
           finisher = *last_flag != 0;
           if (finisher) {
-            __threadfence();
 #pragma unroll
             for (int w = 0; w < NWG; ++w)
 #pragma unroll

@@ -504,11 +504,13 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
               part[j * 128] = make_float4(lo_f(acc[2 * j]), hi_f(acc[2 * j]), lo_f(acc[2 * j + 1]),
                                           hi_f(acc[2 * j + 1]));
           }
-          // Release: the barrier orders every promotion thread's stores before thread 0's fence and increment.
+          // The barrier orders every promotion thread's stores before thread 0's counter increment, one acq_rel
+          // atomic at device scope: its release (cumulative through the barrier) publishes the partials, its
+          // acquire orders the finisher's reads below (after the next barrier).
           named_bar_sync(1, 256);
           if (threadIdx.x == 0) {
-            __threadfence();
-            const int prev = atomicAdd(&p.cnt[tile], 1);
+            int prev;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(p.cnt + tile) : "memory");
             const int last = prev == c_last - c_first;
             if (last) p.cnt[tile] = 0;
             *last_flag = last;
@@ -517,7 +519,6 @@ __global__ void __launch_bounds__(PrefillCfg<FUSED, PAIR>::kThreads, 1)
           // (thread 0 rewrites the flag only after the first barrier of a later shared segment, which every
           // thread reaches after this read)
           if (*last_flag == 0) continue;
-          __threadfence();
 #pragma unroll
           for (int i = 0; i < 64; ++i) acc[i] = 0;
           for (int cc = c_first; cc <= c_last; ++cc) {
