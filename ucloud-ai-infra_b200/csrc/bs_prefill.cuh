@@ -44,8 +44,8 @@ struct GemmParams {
   const float* Bs;   // [N/128, KB] weight block scales
   void* out;         // plain: C [M, ldc]; fused: Q e4m3 [M, I]
   float* qs;         // fused: Qs [M, I/128]
-  float* ws;         // decode split-K partials
-  int* cnt;          // decode split-K arrival counters, one per tile, zero between launches
+  float* ws;         // decode split-K and stream-K prefill partials
+  int* cnt;          // their arrival counters, one per tile, zero between launches
   int* status;       // library status word
   int out_mc;        // plain bf16: `out` is a multicast address; tiles are added into every rank's copy
 };
