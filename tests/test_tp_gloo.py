@@ -133,3 +133,17 @@ def test_tp2_gloo_matches_single_rank():
     assert O.norm_rel_error(out_bf16.float(), ref) <= 4e-3
     # row chunks with their own collectives give the same result as one collective
     assert torch.equal(out_chunked, out_bf16)
+
+
+def test_reduce_mode_contract():
+    """The constructor's rules, on one CPU process (no process group): an unknown reduction is refused, the
+    switch and multicast reductions add bf16 partials only, and without a process group every mode falls back to
+    the single-rank path."""
+    from fp8_hand_b200 import tp
+    with pytest.raises(ValueError):
+        tp.TensorParallelMLP(None, reduce="ring", compute=OracleCompute)
+    for mode in ("switch", "multimem"):
+        with pytest.raises(ValueError):
+            tp.TensorParallelMLP(None, reduce=mode, partial_dtype=torch.float32, compute=OracleCompute)
+        mlp = tp.TensorParallelMLP(None, reduce=mode, compute=OracleCompute)
+        assert (mlp.world, mlp.rank, mlp.reduce) == (1, 0, "nccl")
